@@ -1,0 +1,410 @@
+// fa_b200.cu -- the C ABI (include/fa_b200.h): argument checks, TMA tensor
+// maps, kernel launches on the caller's stream, and the device error word.
+//
+// Host-side counterpart of the reference's torch binding
+// (fa_p100_ext.cu:31-147): the same validation (fa_p100_ext.cu:55-65,
+// :106-115) reported as status codes instead of TORCH_CHECK, the same
+// scale = 1/sqrt(D) (:71, :117) and GROUP = Hq / Hkv (:66), but no allocation
+// (the caller owns every buffer) and an explicit stream instead of the legacy
+// default stream (flash_fwd.cuh:350).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/fa_b200.h"
+#include "fa_bwd.cuh"
+#include "fa_fwd.cuh"
+
+namespace fab {
+
+// Device error word: set by a kernel whose bounded wait gave up.
+__device__ int g_device_error;
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int status = FA_B200_OK;
+  int* err = nullptr;  // address of g_device_error on this device
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+EncodeTiledFn g_encode = nullptr;
+
+// Detail of the most recent failure on this host thread (fa_b200_last_error).
+thread_local char g_last_error[512] = "";
+
+void set_last_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
+void set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+template <typename K>
+void set_smem(K kernel, int bytes) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// One-time, per-device set-up with that device current: architecture check,
+// opt-in to large dynamic shared memory, and the error word's address.
+int device_setup(int* dev_out, int** err_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA_B200_ERR_DEVICE;
+  // Bind the device's primary context to this host thread. The tensor-map
+  // encoder is a driver call and needs a current context; a caller's worker
+  // thread (torch's autograd thread, for one) may not have one yet.
+  if (cudaSetDevice(dev) != cudaSuccess) return FA_B200_ERR_DEVICE;
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.ready) {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (major != 10) {
+      st.status = FA_B200_ERR_DEVICE;
+    } else {
+      if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+          g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+      }
+      void* addr = nullptr;
+      if (!g_encode || cudaGetSymbolAddress(&addr, g_device_error) != cudaSuccess) {
+        st.status = FA_B200_ERR_DEVICE;
+      } else {
+        st.err = static_cast<int*>(addr);
+        set_smem(fwd_kernel<64>, FwdCfg<64>::SMEM);
+        set_smem(fwd_kernel<128>, FwdCfg<128>::SMEM);
+        set_smem(bwd_dkdv_kernel<64>, DkdvCfg<64>::SMEM);
+        set_smem(bwd_dkdv_kernel<128>, DkdvCfg<128>::SMEM);
+        set_smem(bwd_dq_kernel<64>, DqCfg<64>::SMEM);
+        set_smem(bwd_dq_kernel<128>, DqCfg<128>::SMEM);
+        st.status = (cudaGetLastError() == cudaSuccess) ? FA_B200_OK : FA_B200_ERR_DEVICE;
+      }
+    }
+    st.ready = true;
+  }
+  *err_out = st.err;
+  return st.status;
+}
+
+// 3-D fp16 (or fp32) tensor (slices, rows, cols) with 128-byte swizzled boxes
+// of box_rows x (128 bytes of columns). Rows past `rows` read as zero.
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
+              uint64_t cols, uint64_t rows, uint64_t slices, uint32_t box_rows) {
+  const cuuint64_t dims[3] = {cols, rows, slices};
+  const cuuint64_t strides[2] = {cols * elem_bytes, cols * rows * elem_bytes};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / elem_bytes), box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = g_encode(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_last_error(
+        "cuTensorMapEncodeTiled -> CUresult %d for base %p (map at %p), dims {%llu, %llu, %llu}, "
+        "strides {%llu, %llu} bytes, box {%u, %u, 1}",
+        static_cast<int>(r), base, static_cast<void*>(m), static_cast<unsigned long long>(cols),
+        static_cast<unsigned long long>(rows), static_cast<unsigned long long>(slices),
+        static_cast<unsigned long long>(strides[0]), static_cast<unsigned long long>(strides[1]),
+        box[0], box[1]);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_shape(int B, int Hq, int Hkv, int N, int D) {
+  if (D != 64 && D != 128) return FA_B200_ERR_HEAD_DIM;
+  if (B < 1 || N < 1 || Hkv < 1 || Hq < 1 || Hq % Hkv != 0) return FA_B200_ERR_SHAPE;
+  return FA_B200_OK;
+}
+
+template <int D>
+int launch_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                   int Hkv, int N, int causal, cudaStream_t stream, int* err) {
+  using C = FwdCfg<D>;
+  CUtensorMap tq, tk, tv;
+  const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
+  if (!make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
+      !make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
+      !make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128))
+    return FA_B200_ERR_TENSOR_MAP;
+  FwdParams p;
+  p.o = static_cast<__half*>(o);
+  p.lse = lse;
+  p.err = err;
+  p.n = N;
+  p.hq = Hq;
+  p.group = Hq / Hkv;
+  p.causal = causal ? 1 : 0;
+  p.n_mblocks = (N + 255) / 256;
+  p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
+  if (p.n_mblocks > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
+  dim3 grid(static_cast<unsigned>(BH), p.n_mblocks);
+  fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? FA_B200_OK : FA_B200_ERR_LAUNCH;
+}
+
+template <int D>
+int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
+                    const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* dvec, int B,
+                    int Hq, int Hkv, int N, int causal, cudaStream_t stream, int* err) {
+  const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
+  const int nq128 = (N + 127) / 128;
+  if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
+  // Q/dO boxes are 64 rows for the key-stationary kernel, 128 for the dQ kernel.
+  CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
+  if (!make_map(&tq64, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 64) ||
+      !make_map(&tdo64, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 64) ||
+      !make_map(&tk128, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
+      !make_map(&tv128, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
+      !make_map(&tq128, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
+      !make_map(&tdo128, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
+      !make_map(&tk64, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 64) ||
+      !make_map(&tv64, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 64))
+    return FA_B200_ERR_TENSOR_MAP;
+  BwdParams p;
+  p.o = static_cast<const __half*>(o);
+  p.dO = static_cast<const __half*>(dO);
+  p.lse = lse;
+  p.dvec = dvec;
+  p.dq = dq;
+  p.dk = static_cast<__half*>(dk);
+  p.dv = static_cast<__half*>(dv);
+  p.err = err;
+  p.n = N;
+  p.hq = Hq;
+  p.group = Hq / Hkv;
+  p.causal = causal ? 1 : 0;
+  p.dq_fp32 = dq_fp32 ? 1 : 0;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
+  p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
+
+  const long long rows = static_cast<long long>(BH) * N;
+  const long long threads = rows * (D / 8);
+  bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+      static_cast<const __half*>(o), static_cast<const __half*>(dO), dvec, rows);
+  if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
+                       DkdvCfg<D>::SMEM, stream>>>(tq64, tk128, tv128, tdo64, p);
+  if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
+                     stream>>>(tq128, tk64, tv64, tdo128, p);
+  return cudaGetLastError() == cudaSuccess ? FA_B200_OK : FA_B200_ERR_LAUNCH;
+}
+
+}  // namespace
+}  // namespace fab
+
+namespace fab {
+
+// One 128x128x128 tile: c = A * B^T through the production layouts.
+// Threads 0-127 read TMEM rows; thread 160 (warp 5) issues TMA; thread 128
+// (warp 4) allocates TMEM and issues the MMAs.
+__global__ void __launch_bounds__(192, 1)
+    selftest_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                         const __half* a_raw, float* c, int a_mn, int b_mn, int a_by_threads,
+                         int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t s_a = sbase, s_b = sbase + 32768;
+  const uint32_t b_ld = sbase + 65536, b_mma = b_ld + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + 65536 + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5;
+  const Ctl ctl{abort_flag, err};
+  if (threadIdx.x == 0) {
+    mbar_init(b_ld, 1);
+    mbar_init(b_mma, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) tmem_alloc(smem_u32(tmem_slot), 128);
+  if (a_by_threads && threadIdx.x < 128) {
+    // A is [M][K]; thread m writes its row into the swizzled K-major layout.
+    const int m = threadIdx.x;
+    for (int c8 = 0; c8 < 16; ++c8) {
+      const uint4 v = reinterpret_cast<const uint4*>(a_raw + m * 128)[c8];
+      st_shared_v4(s_a + sw128_offset(m, c8, 128), v.x, v.y, v.z, v.w);
+    }
+    fence_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 160) {
+    mbar_arrive_expect_tx(b_ld, a_by_threads ? 32768 : 65536);
+    for (int ch = 0; ch < 2; ++ch) {
+      if (!a_by_threads) tma_load_3d(s_a + ch * 16384, &ta, b_ld, ch * 64, 0, 0);
+      tma_load_3d(s_b + ch * 16384, &tb, b_ld, ch * 64, 0, 0);
+    }
+  }
+  if (threadIdx.x == 128) {
+    if (mbar_wait(b_ld, 0, ctl, kErrTimeoutMma)) {
+      tc_fence_after();
+      const uint32_t id = idesc_f16(128, 128, a_mn != 0, b_mn != 0);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;  // K-major step
+        const uint64_t da = a_mn ? sdesc_sw128(s_a + kk * 2048, 16384, 1024)
+                                 : sdesc_sw128(s_a + koff, 16, 1024);
+        const uint64_t db = b_mn ? sdesc_sw128(s_b + kk * 2048, 16384, 1024)
+                                 : sdesc_sw128(s_b + koff, 16, 1024);
+        mma_ss(tmem, da, db, id, kk > 0 ? 1u : 0u);
+      }
+      mma_commit(b_mma);
+    } else {
+      drain_loads(b_ld, 1, 1);
+    }
+  }
+  if (threadIdx.x < 128) {
+    bool ok = mbar_wait(b_mma, 0, ctl, kErrTimeoutEpilogue);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t v[32];
+        tmem_ld32(tmem + 32 * ch + lane_off, v);
+        tmem_ld_wait(v);
+        for (int i = 0; i < 32; ++i) c[threadIdx.x * 128 + 32 * ch + i] = __uint_as_float(v[i]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) {
+    __syncwarp();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+}  // namespace fab
+
+// ===========================================================================
+// extern "C" entry points
+// ===========================================================================
+extern "C" {
+
+int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                    int Hkv, int N, int D, int causal, int full_precision, void* stream) {
+  (void)full_precision;
+  if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
+  int st = fab::check_shape(B, Hq, Hkv, N, D);
+  if (st != FA_B200_OK) return st;
+  if (!fab::aligned16(q) || !fab::aligned16(k) || !fab::aligned16(v) || !fab::aligned16(o) ||
+      !fab::aligned16(lse))
+    return FA_B200_ERR_ALIGNMENT;
+  int dev = 0;
+  int* err = nullptr;
+  st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  return D == 64 ? fab::launch_forward<64>(q, k, v, o, lse, B, Hq, Hkv, N, causal, s, err)
+                 : fab::launch_forward<128>(q, k, v, o, lse, B, Hq, Hkv, N, causal, s, err);
+}
+
+size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {
+  if (B < 1 || Hq < 1 || N < 1) return 0;
+  // rounded up to 256 bytes so a caller can carve further buffers after it
+  const size_t bytes = static_cast<size_t>(B) * Hq * N * sizeof(float);
+  return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
+int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
+                     const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
+                     size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
+                     void* stream) {
+  if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
+  int st = fab::check_shape(B, Hq, Hkv, N, D);
+  if (st != FA_B200_OK) return st;
+  if (!workspace || workspace_bytes < fa_b200_backward_workspace_bytes(B, Hq, N))
+    return FA_B200_ERR_WORKSPACE;
+  const void* ptrs[] = {q, k, v, dO, o, lse, dq, dk, dv, workspace};
+  for (const void* ptr : ptrs)
+    if (!fab::aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
+  int dev = 0;
+  int* err = nullptr;
+  st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  float* dvec = static_cast<float*>(workspace);
+  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                                            Hkv, N, causal, s, err)
+                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                                             Hkv, N, causal, s, err);
+}
+
+int fa_b200_device_error(int device, int reset) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return -1;
+  if (cudaSetDevice(device) != cudaSuccess) return -1;
+  int value = -1;
+  if (cudaDeviceSynchronize() == cudaSuccess &&
+      cudaMemcpyFromSymbol(&value, fab::g_device_error, sizeof(int)) == cudaSuccess && reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(fab::g_device_error, &zero, sizeof(int)) != cudaSuccess) value = -1;
+  }
+  cudaSetDevice(prev);
+  return value;
+}
+
+const char* fa_b200_last_error(void) { return fab::g_last_error; }
+
+const char* fa_b200_status_string(int status) {
+  switch (status) {
+    case FA_B200_OK: return "ok";
+    case FA_B200_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case FA_B200_ERR_HEAD_DIM: return "head dim must be 64 or 128";
+    case FA_B200_ERR_SHAPE: return "bad shape: need B, N, Hkv >= 1 and Hq a multiple of Hkv";
+    case FA_B200_ERR_ALIGNMENT: return "device pointers must be 16-byte aligned";
+    case FA_B200_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled rejected a tensor";
+    case FA_B200_ERR_LAUNCH: return "kernel launch failed";
+    case FA_B200_ERR_WORKSPACE: return "workspace missing or too small";
+    case FA_B200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case FA_B200_ERR_TOO_LARGE: return "problem exceeds a CUDA grid limit";
+    default: return "unknown status";
+  }
+}
+
+int fa_b200_selftest_gemm(const void* a, const void* b, float* c, int a_mn, int b_mn,
+                          int a_by_threads, void* stream) {
+  if (!a || !b || !c) return FA_B200_ERR_NULL_POINTER;
+  if (!fab::aligned16(a) || !fab::aligned16(b) || !fab::aligned16(c)) return FA_B200_ERR_ALIGNMENT;
+  if (a_by_threads && a_mn) return FA_B200_ERR_SHAPE;
+  int dev = 0;
+  int* err = nullptr;
+  int st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  CUtensorMap ta, tb;
+  if (!fab::make_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128, 128, 1, 128) ||
+      !fab::make_map(&tb, b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128, 128, 1, 128))
+    return FA_B200_ERR_TENSOR_MAP;
+  constexpr int smem = 65536 + 64 + 1024;
+  cudaFuncSetAttribute(fab::selftest_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  fab::selftest_gemm_kernel<<<1, 192, smem, static_cast<cudaStream_t>(stream)>>>(
+      ta, tb, static_cast<const __half*>(a), c, a_mn, b_mn, a_by_threads, err);
+  return cudaGetLastError() == cudaSuccess ? FA_B200_OK : FA_B200_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,376 @@
+// fa_fwd.cuh -- FlashAttention-2 forward for sm_100a.
+//
+// Replaces flash::fwd_kernel / flash::launch (reference flash_fwd.cuh:68-355).
+// Same math: O = softmax(scale * Q K^T + mask) V with the scale applied to the
+// fp32 logit (flash_fwd.cuh:94-103, :220-224), causal and ragged-tail columns
+// masked to -inf (:226-243), blocks wholly above the diagonal never visited
+// (:127-130), LSE = m + ln(l) in natural log (:321-330), GQA head mapping
+// kv_head = q_head / group (:87-92).
+//
+// Structure of one CTA (persistent over nothing: one CTA = 256 query rows of
+// one (batch, q-head)):
+//   warps 0-3  softmax for query tile 0 (rows m0 .. m0+127), one thread per row
+//   warps 4-7  softmax for query tile 1 (rows m0+128 .. m0+255)
+//   warp  8    TMEM allocation + the single thread that issues tcgen05.mma
+//   warp  9    the single thread that issues TMA loads
+// TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
+// Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate), P0, P1.
+//
+// Per key block j the MMA thread issues, in order,
+//   PV0_{j-1}... S0_j = Q0 K_j^T ; S1_j = Q1 K_j^T ; [P0_j] O0 += P0_j V_j ;
+//   S0_{j+1} ; [P1_j] O1 += P1_j V_j ; S1_{j+1} ; ...
+// so the tensor core computes one tile's S while the other tile's softmax runs.
+// tcgen05.commit tracks every MMA issued before it, so when softmax t sees
+// S_t,j+1 complete, PV_t,j is complete too: P_t's buffer and O_t are free to
+// rewrite, and no extra barrier is needed for either.
+#pragma once
+#include "sm100.cuh"
+
+namespace fab {
+
+struct FwdParams {
+  __half* o;        // (B*Hq, N, D)
+  float* lse;       // (B*Hq, N), natural log
+  int* err;         // device error word
+  int n;            // sequence length
+  int hq;           // query heads
+  int group;        // hq / hkv
+  int causal;
+  int n_mblocks;    // ceil(N / 256)
+  float scale_log2; // softmax scale * log2(e)
+};
+
+template <int D>
+struct FwdCfg {
+  static constexpr int BM = 128;                // rows per query tile
+  static constexpr int BN = 128;                // keys per block
+  static constexpr int CH = D / 64;             // 64-column chunks per row
+  static constexpr int QBYTES = BM * D * 2;
+  static constexpr int KVBYTES = BN * D * 2;
+  static constexpr int PBYTES = BM * BN * 2;
+  static constexpr int STAGES = (D == 128) ? 3 : 6;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
+  static constexpr int OFF_P = OFF_RING + STAGES * KVBYTES;
+  static constexpr int OFF_BAR = OFF_P + 2 * PBYTES;
+  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin; then tmem addr + abort flag
+  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
+  static constexpr int THREADS = 320;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O0 = 256, COL_O1 = 256 + D;
+};
+
+}  // namespace fab
+
+namespace fab {
+
+// ---------------------------------------------------------------------------
+// MMA issue helpers (single thread)
+// ---------------------------------------------------------------------------
+// S[tmem] = Q_tile (128 x D, K-major) * K_tile^T (128 x D, K-major)
+template <int D>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t k_s) {
+  constexpr uint32_t idesc = idesc_f16(128, 128, false, false);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+    mma_ss(d_tmem, sdesc_sw128(q_s + off, 16, 1024), sdesc_sw128(k_s + off, 16, 1024), idesc,
+           kk > 0 ? 1u : 0u);
+  }
+}
+// O[tmem] (+)= P (128 x 128 keys, K-major) * V (128 keys x D, MN-major)
+template <int D>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_s, uint32_t v_s,
+                                         bool accumulate) {
+  constexpr uint32_t idesc = idesc_f16(128, D, false, true);
+#pragma unroll
+  for (int kk = 0; kk < 128 / 16; ++kk) {
+    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+    mma_ss(d_tmem, sdesc_sw128(p_s + aoff, 16, 1024), sdesc_sw128(v_s + kk * 2048, 16384, 1024),
+           idesc, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+
+  const uint32_t s_q0 = sbase + C::OFF_Q, s_q1 = s_q0 + C::QBYTES;
+  const uint32_t s_ring = sbase + C::OFF_RING;
+  const uint32_t s_p0 = sbase + C::OFF_P, s_p1 = s_p0 + C::PBYTES;
+  const uint32_t b_q = sbase + C::OFF_BAR;
+  const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
+  const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 16;
+  const uint32_t b_fin = b_o + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // grid (B*Hq, m-blocks): every head's longest causal rows are dispatched first
+  const int bh = blockIdx.x;
+  const int mb = p.causal ? (p.n_mblocks - 1 - static_cast<int>(blockIdx.y)) : static_cast<int>(blockIdx.y);
+  const int m0 = mb * 256;
+  const int kvh = (bh / p.hq) * (p.hq / p.group) + (bh % p.hq) / p.group;
+  const int nblk = (p.n + 127) / 128;
+  int ntile[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int r0 = m0 + 128 * t;
+    ntile[t] = (r0 >= p.n) ? 0 : (p.causal ? min(nblk, r0 / 128 + 1) : nblk);
+  }
+  const int nkv = max(ntile[0], ntile[1]);
+  const Ctl ctl{abort_flag, p.err};
+
+  if (threadIdx.x == 0) {
+    mbar_init(b_q, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(b_full + 8 * s, 1);
+      mbar_init(b_empty + 8 * s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(b_s + 8 * t, 1);
+      mbar_init(b_p + 8 * t, 128);
+      mbar_init(b_o + 8 * t, 1);
+    }
+    mbar_init(b_fin, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(b_q, 2 * C::QBYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < C::CH; ++c)
+          tma_load_3d((t ? s_q1 : s_q0) + c * 16384, &tm_q, b_q, c * 64, m0 + 128 * t, bh);
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < nkv && ok; ++j) {
+#pragma unroll 1
+        for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
+          const int slot = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          ok = mbar_wait(b_empty + 8 * slot, ph ^ 1, ctl, kErrTimeoutLoad);
+          if (!ok) break;
+          const uint32_t fb = b_full + 8 * slot;
+          mbar_arrive_expect_tx(fb, C::KVBYTES);
+          const uint32_t dst = s_ring + slot * C::KVBYTES;
+#pragma unroll
+          for (int c = 0; c < C::CH; ++c)
+            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
+                        c * 64, j * 128, kvh);
+        }
+      }
+      // Drain: do not leave the CTA while a load it issued may still land.
+      if (!ok) {
+        drain_loads(b_q, 1, 1);
+        drain_loads(b_full, it, C::STAGES);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(b_q, 0, ctl, kErrTimeoutMma);
+      int it = 0;
+      if (ok && nkv > 0) {
+        // prologue: S_t,0 for both tiles
+        ok = mbar_wait(b_full, 0, ctl, kErrTimeoutMma);
+        if (ok) {
+          tc_fence_after();
+#pragma unroll
+          for (int t = 0; t < 2; ++t)
+            if (ntile[t] > 0) {
+              issue_qk<D>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0, s_ring);
+              mma_commit(b_s + 8 * t);
+            }
+          mma_commit(b_empty);
+          it = 1;
+        }
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int slot_v = it % C::STAGES;
+        ok = mbar_wait(b_full + 8 * slot_v, (it / C::STAGES) & 1, ctl, kErrTimeoutMma);
+        ++it;
+        if (!ok) break;
+        tc_fence_after();
+        const bool more = (j + 1 < nkv);
+        const int slot_k = it % C::STAGES;
+        const uint32_t ph_k = (it / C::STAGES) & 1;
+        if (more) ++it;
+        bool have_k = false;
+#pragma unroll
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= ntile[t]) continue;
+          ok = mbar_wait(b_p + 8 * t, j & 1, ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0), t ? s_p1 : s_p0,
+                      s_ring + slot_v * C::KVBYTES, j > 0);
+          if (j + 1 < ntile[t]) {
+            if (!have_k) {
+              ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
+              if (!ok) break;
+              tc_fence_after();
+              have_k = true;
+            }
+            issue_qk<D>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0,
+                        s_ring + slot_k * C::KVBYTES);
+            mma_commit(b_s + 8 * t);
+          } else {
+            mma_commit(b_o + 8 * t);  // last block of this tile: O_t is final
+          }
+        }
+        if (!ok) break;
+        mma_commit(b_empty + 8 * slot_v);
+        if (more) {
+          if (!have_k) {
+            ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
+            if (!ok) break;
+          }
+          mma_commit(b_empty + 8 * slot_k);
+        }
+      }
+      // Every MMA issued above must finish before TMEM is released.
+      mma_commit(b_fin);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(b_fin, 0) && globaltimer_ns() - t0 < FAB_WAIT_LIMIT_NS) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax tile t
+    const int t = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const int row = m0 + 128 * t + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
+    const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
+    const uint32_t s_p = t ? s_p1 : s_p0;
+    const int nt = ntile[t];
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      ok = mbar_wait(b_s + 8 * t, j & 1, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, sr[c]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+      float* s = reinterpret_cast<float*>(&sr[0][0]);
+      const int col0 = j * 128;
+      const bool need_mask = (col0 + 128 > p.n) || (p.causal && col0 + 127 > m0 + 128 * t);
+      if (need_mask) {
+        const int lim = p.causal ? min(p.n - 1, row) : (p.n - 1);
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (col0 + c > lim) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      const float m_new = fmaxf(m_used, mx * p.scale_log2);
+      if (j == 0) {
+        m_used = m_new;
+      } else {
+        // Rescale only when the running max grew by more than 2^8: P stays
+        // below 256, and the final 1/l uses the same offset, so the result is
+        // unchanged (only which power of two the partial sums carry).
+        const bool need = m_new > m_used + 8.f;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2(m_used - m_new) : 1.f;
+          if (need) {
+            l *= alpha;
+            m_used = m_new;
+          }
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(t_o + 32 * c, orow);
+            tmem_ld_wait(orow);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            tmem_st32(t_o + 32 * c, orow);
+          }
+          tmem_st_wait();
+        }
+      }
+      const float moff = m_used;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float e0 = ex2(fmaf(s[8 * c8 + 2 * h], p.scale_log2, -moff));
+          const float e1 = ex2(fmaf(s[8 * c8 + 2 * h + 1], p.scale_log2, -moff));
+          l += e0 + e1;
+          w[h] = pack_half2(e0, e1);
+        }
+        st_shared_v4(s_p + sw128_offset(r, c8, 128), w[0], w[1], w[2], w[3]);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(b_p + 8 * t);
+    }
+    if (ok && nt > 0) {
+      ok = mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float inv = 1.f / l;
+        const size_t bhn = static_cast<size_t>(bh) * p.n;
+        __half* orow_g = p.o + (bhn + row) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t orow[32];
+          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld_wait(orow);
+          if (row < p.n) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 pk;
+              pk.x = pack_half2(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
+              pk.y = pack_half2(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
+              pk.z = pack_half2(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
+              pk.w = pack_half2(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow_g + 32 * c + 8 * v) = pk;
+            }
+          }
+        }
+        if (row < p.n) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8) {
+    __syncwarp();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fab

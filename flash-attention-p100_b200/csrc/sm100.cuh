@@ -1,0 +1,276 @@
+// sm100.cuh -- thin, hand-written wrappers over the Blackwell (sm_100a) PTX used by
+// the attention kernels: mbarriers with bounded waits, TMA tile loads, tcgen05
+// tensor-memory allocation / MMA / load / store, and the shared-memory and
+// instruction descriptors the MMAs read.
+//
+// Layout conventions used everywhere in this library
+// ---------------------------------------------------
+// Every fp16 operand tile lives in shared memory in the canonical 128-byte
+// swizzled layout that a TMA load with CU_TENSOR_MAP_SWIZZLE_128B writes:
+//   * a tile of R rows x 64 fp16 (one "chunk", 128 B per row) occupies R*128 B;
+//   * row r starts at r*128; its 16-byte piece c sits at ((c ^ (r & 7)) * 16);
+//   * a D=128 tile is two chunk regions back to back (columns 0-63, 64-127).
+// Read as an MMA operand, the same bytes serve two roles:
+//   * K-major  (contraction index = the 64-wide column):  SBO = 1024 B between
+//     8-row groups, a K step of 16 elements = +32 B inside a chunk, next chunk =
+//     +R*128 B;
+//   * MN-major (contraction index = the row):  LBO = R*128 B between 64-wide
+//     chunks of the M/N index, SBO = 1024 B between 8-row groups, a K step of
+//     16 rows = +2048 B.
+// TMEM accumulators of an M=128 MMA put row m in lane m and column n in
+// TMEM column n (fp32). Warp w of a CTA may only touch lanes 32*(w%4)..+31.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace fab {
+
+// ---------------------------------------------------------------------------
+// error reporting: a device-global word the host can read and clear
+// ---------------------------------------------------------------------------
+enum DevErr : int {
+  kErrNone = 0,
+  kErrTimeoutLoad = 1,   // producer waited too long for a free ring slot
+  kErrTimeoutMma = 2,    // MMA issuer waited too long for an operand
+  kErrTimeoutSoftmax = 3,  // softmax / compute warps waited too long for an MMA
+  kErrTimeoutEpilogue = 4,
+};
+
+// One wait gives up after this many nanoseconds of global time. Every healthy
+// wait in these kernels is microseconds; a second means the pipeline is stuck.
+#ifndef FAB_WAIT_LIMIT_NS
+#define FAB_WAIT_LIMIT_NS 1000000000ull
+#endif
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Shared state every role checks so that one stuck wait stops the whole CTA.
+struct Ctl {
+  volatile int* abort_flag;  // in shared memory
+  int* err;                  // device-global error word (may be null)
+};
+
+// Wait for the phase with the given parity to complete. Returns false (and
+// records `code`) if the wait exceeded FAB_WAIT_LIMIT_NS, or if another role of
+// this CTA already gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Ctl& ctl, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*ctl.abort_flag) return false;
+    if (globaltimer_ns() - t0 > FAB_WAIT_LIMIT_NS) {
+      *ctl.abort_flag = 1;
+      if (ctl.err) atomicCAS(ctl.err, 0, code);
+      return false;
+    }
+  }
+}
+
+// After a failed wait, a producer that issued loads 0..issued-1 into a ring of
+// `stages` slots waits (bounded, 100 ms per slot) for the ones that may still
+// be in flight, so no TMA write lands in shared memory after the CTA exits.
+__device__ __forceinline__ void drain_loads(uint32_t full_bars, int issued, int stages) {
+  for (int it = (issued > stages ? issued - stages : 0); it < issued; ++it) {
+    const uint32_t bar = full_bars + 8 * (it % stages);
+    const uint32_t parity = (it / stages) & 1;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity) && globaltimer_ns() - t0 < 100000000ull) {
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fences
+// ---------------------------------------------------------------------------
+// Generic-proxy shared-memory writes -> visible to the async proxy (TMA, MMA).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMA (no multicast anywhere in this library)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+// 3-D tiled load: coordinates are (inner column, row, head-slice).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory
+// ---------------------------------------------------------------------------
+// Whole warp. Writes the allocated TMEM base address into *dst_smem.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 (version 1).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulation.
+// a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4)                                    // D format: f32
+         | (0u << 7) | (0u << 10)                     // A, B: f16
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
+         | (static_cast<uint32_t>(N >> 3) << 17)      // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);     // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]. Issued by one thread.
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05.ld / st, 32 lanes x 32 bit, 32 consecutive columns per thread
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// Wait for this thread's outstanding tcgen05.ld, then pin the loaded registers
+// after the wait so the compiler cannot read them early.
+template <int NR>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[NR]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(r[i]));
+}
+__device__ __forceinline__ void tmem_ld_wait_only() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// small helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of 16-byte piece `c` (0..D/8-1) of row `r` in a swizzled tile of
+// `rows` rows (see the layout note at the top of this file).
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c, int rows) {
+  return static_cast<uint32_t>((c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+}  // namespace fab

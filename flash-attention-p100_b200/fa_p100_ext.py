@@ -1,0 +1,110 @@
+"""The extension ops `forward` / `backward`, same names and contract as the
+reference's pybind11 module (fa_p100_ext.cu:144-147), implemented over the C ABI
+of libfa_b200.so (include/fa_b200.h).
+
+    forward(q, k, v, causal, full_precision) -> [o, lse]
+    backward(q, k, v, dO, o, lse, causal)    -> [dq (fp32), dk, dv]
+
+Validation and messages follow fa_p100_ext.cu:31-35, :55-65, :106-115 and raise
+RuntimeError, as TORCH_CHECK does. Outputs and the row-sum workspace are
+allocated here with torch on the inputs' device (fa_p100_ext.cu:68-69,
+:121-124); kernels run on torch's current CUDA stream rather than the legacy
+default stream. There is no CPU path: CPU tensors are rejected.
+"""
+import math
+
+import torch
+
+import _lib
+
+
+def _check_in(t, name):
+    # fa_p100_ext.cu:31-35
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be fp16")
+    if t.dim() != 4:
+        raise RuntimeError(f"{name} must be (B, H, N, D)")
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _shapes(q, k, v):
+    B, H, N, D = q.shape
+    Hkv = k.size(1)
+    if D not in (64, 128):
+        raise RuntimeError(f"head dim must be 64 or 128, got {D}")
+    if N <= 0:
+        raise RuntimeError("N must be positive")
+    if not (Hkv > 0 and H % Hkv == 0):
+        raise RuntimeError(
+            f"query heads ({H}) must be a multiple of key/value heads ({Hkv})")
+    if k.shape != v.shape:
+        raise RuntimeError("k and v must match")
+    if k.size(0) != B or k.size(2) != N or k.size(3) != D:
+        raise RuntimeError("k/v must be (B, Hkv, N, D) matching q's B, N, D")
+    return B, H, Hkv, N, D
+
+
+def forward(q, k, v, causal, full_precision=False):
+    """O (B,Hq,N,D) fp16 and LSE (B,Hq,N) fp32 (natural log). fa_p100_ext.cu:53-83."""
+    _check_in(q, "q")
+    _check_in(k, "k")
+    _check_in(v, "v")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    B, H, Hkv, N, D = _shapes(q, k, v)
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        st = _lib.lib().fa_b200_forward(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+            B, H, Hkv, N, D, 1 if causal else 0, 1 if full_precision else 0,
+            _stream_ptr(q.device))
+    _lib.check(st, "fa_b200_forward")
+    return [o, lse]
+
+
+def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32):
+    """dq (dq_dtype), dk, dv. `dq_dtype` fp16 lets autograd skip the fp32 copy."""
+    _check_in(q, "q")
+    _check_in(dO, "dO")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    dO, o, lse = dO.contiguous(), o.contiguous(), lse.contiguous()
+    # fa_p100_ext.cu:106-115 checks only q and dO; k, v, o and lse are checked
+    # here too, because a wrong dtype would be read as garbage by the kernels.
+    for t, name in ((k, "k"), (v, "v"), (o, "o")):
+        _check_in(t, name)
+    if lse.dtype != torch.float32 or not lse.is_cuda:
+        raise RuntimeError("lse must be a CUDA fp32 tensor")
+    B, H, Hkv, N, D = _shapes(q, k, v)
+    if dO.shape != q.shape or o.shape != q.shape or lse.shape != (B, H, N):
+        raise RuntimeError("dO and o must match q, and lse must be (B, Hq, N)")
+    if dq_dtype not in (torch.float32, torch.float16):
+        raise RuntimeError("dq_dtype must be float32 or float16")
+    dq = torch.empty((B, H, N, D), device=q.device, dtype=dq_dtype)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(k)
+    lib = _lib.lib()
+    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
+    ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        st = lib.fa_b200_backward(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), dO.data_ptr(), o.data_ptr(),
+            lse.data_ptr(), dq.data_ptr(), 1 if dq_dtype == torch.float32 else 0,
+            dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
+            B, H, Hkv, N, D, 1 if causal else 0, _stream_ptr(q.device))
+    _lib.check(st, "fa_b200_backward")
+    return [dq, dk, dv]
+
+
+def backward(q, k, v, dO, o, lse, causal):
+    """dq fp32 (B,Hq,N,D), dk, dv fp16 (B,Hkv,N,D). fa_p100_ext.cu:103-142."""
+    return backward_into(q, k, v, dO, o, lse, causal, torch.float32)
+
+
+def softmax_scale(head_dim):
+    """The scale every kernel uses: 1/sqrt(D) (fa_p100_ext.cu:71, :117)."""
+    return 1.0 / math.sqrt(head_dim)

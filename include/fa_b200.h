@@ -1,0 +1,91 @@
+/* fa_b200.h -- C ABI of the B200 (sm_100a) FlashAttention-2 library.
+ *
+ * Plain pointers, sizes and a CUDA stream: no torch or C++ types cross this
+ * boundary. Every tensor is dense row-major (contiguous), fp16 unless stated:
+ *   q, o, dO, dq   (B, Hq,  N, D)
+ *   k, v, dk, dv   (B, Hkv, N, D)
+ *   lse            (B, Hq,  N)  fp32, natural log: lse = m + ln(sum exp(s - m))
+ * with D in {64, 128}, N >= 1, Hq a multiple of Hkv (Hkv == Hq: MHA, 1: MQA,
+ * otherwise GQA), scale fixed at 1/sqrt(D), and causal meaning key j is
+ * visible to query i iff j <= i. All device pointers must be 16-byte aligned.
+ *
+ * Ownership: the caller allocates every buffer (outputs and workspace); the
+ * library allocates no device memory. Work is enqueued on `stream` (a
+ * cudaStream_t; NULL = legacy default stream) and the calls return before it
+ * finishes. Calls are thread-safe.
+ *
+ * Every entry point returns an int status (FA_B200_OK = 0). Argument errors
+ * are reported before anything is launched.
+ */
+#ifndef FA_B200_H_
+#define FA_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FA_B200_OK = 0,
+  FA_B200_ERR_NULL_POINTER = 1,    /* a required pointer is NULL */
+  FA_B200_ERR_HEAD_DIM = 2,        /* D not in {64, 128} */
+  FA_B200_ERR_SHAPE = 3,           /* N < 1, B < 1, Hkv < 1, or Hq % Hkv != 0 */
+  FA_B200_ERR_ALIGNMENT = 4,       /* a device pointer is not 16-byte aligned */
+  FA_B200_ERR_TENSOR_MAP = 5,      /* cuTensorMapEncodeTiled rejected a tensor */
+  FA_B200_ERR_LAUNCH = 6,          /* a kernel launch failed (cudaGetLastError) */
+  FA_B200_ERR_WORKSPACE = 7,       /* workspace missing or smaller than required */
+  FA_B200_ERR_DEVICE = 8,          /* current device is not compute capability 10.x */
+  FA_B200_ERR_TOO_LARGE = 9        /* a grid dimension would exceed CUDA limits */
+};
+
+/* Forward. Replaces fa_forward (reference fa_p100_ext.cu:53-83) and
+ * flash::launch (flash_fwd.cuh:342-355): writes o and lse.
+ * `full_precision` is accepted for API compatibility (fa_p100_ext.cu:53) and
+ * has no effect: the tensor-core MMAs multiply fp16 exactly and accumulate in
+ * fp32, which is the reference's fp32-MAC tier. */
+int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float* lse,
+                    int B, int Hq, int Hkv, int N, int D, int causal, int full_precision,
+                    void* stream);
+
+/* Bytes of device workspace fa_b200_backward needs: B*Hq*N fp32 for the
+ * row sums Dv = rowsum(dO o O) (reference fa_p100_ext.cu:124). */
+size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
+
+/* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
+ * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq (fp32 when dq_fp32 != 0,
+ * as the reference returns it, else fp16), dk and dv (fp16). dq is computed
+ * without atomics and is bitwise deterministic. */
+int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
+                     const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
+                     size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
+                     void* stream);
+
+/* Reads the device error word the kernels set when a bounded internal wait
+ * gives up (1..4; 0 = none) on `device`, and clears it when `reset` != 0.
+ * Synchronises that device. Returns -1 if the read itself fails. Has no
+ * counterpart in the reference, whose kernels have no waits. */
+int fa_b200_device_error(int device, int reset);
+
+/* Human-readable text for a status code. */
+const char* fa_b200_status_string(int status);
+
+/* Detail of the most recent failure on the calling host thread (for example
+ * the CUresult and arguments of a rejected tensor map); "" if none. No
+ * counterpart in the reference, whose errors are TORCH_CHECK messages. */
+const char* fa_b200_last_error(void);
+
+/* Layout self-test, no counterpart in the reference: c (128x128 fp32) =
+ * A * B^T for one 128x128x128 fp16 tile through the same TMA swizzle, shared-
+ * memory descriptors and tcgen05 MMA the attention kernels use. a_mn / b_mn
+ * select MN-major operands (a given as [K][M], b as [K][N]); otherwise a is
+ * [M][K] and b is [N][K]. a_by_threads != 0 stages A with thread stores (the
+ * path P and dS take) instead of TMA. */
+int fa_b200_selftest_gemm(const void* a, const void* b, float* c, int a_mn, int b_mn,
+                          int a_by_threads, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H_ */
