@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""Attention fwd+bwd benchmark (BASELINE.json metric: attention fwd+bwd TFLOPS per
+GPU and % of the fp16 tensor peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload C2|C1|C3a|C3b|north_star]
+
+One step = one forward + one backward of the attention hot path over one batch
+of seeded synthetic fp16 inputs (i.i.d. N(0,1), as BASELINE.json's configs say).
+The default workload is configs[1] (C2: B=1, Hq=Hkv=8, N=4096, D=128, causal).
+
+Our arm (--impl ours):
+  value   whole-job TFLOPS with inputs resident in HBM, through the C ABI
+          (fa_b200_forward + fa_b200_backward_stages), L2 flushed (256 MiB
+          write) between steps outside the timed events;
+  e2e     the same metric through the public API (fa_p100.flash_attn + autograd
+          backward) with q, k, v, dO copied from pinned host memory and dq, dk,
+          dv copied back inside the timed region;
+  roofline the dominant kernel's algorithmic FLOPs / its CUDA-event time;
+  cpu_baseline  the reference's CPU path (torch fp32 eager attention, restated
+          in oracle/) on a bounded sample, rank 0 at N=1 only.
+Multi-GPU (torchrun): heads are sharded, each rank runs its own full workload
+with no collective on the data path (weak scaling); time = max over ranks.
+
+The reference arm (--impl reference) times the reference's CPU implementation
+of the path (fa_p100.reference, restated in oracle/attention_oracle.py) on the
+host cores, rank 0 only.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "flash-attention-p100_b200")
+for _p in (PKG, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "attn fwd+bwd TFLOPS/GPU & % of fp16 tensor peak; Qwen3-0.6B-shape step ms"
+UNIT = "TFLOPS"
+WORKLOADS = {
+    # name: (B, Hq, Hkv, N, D, causal, input scale)
+    "C1": (1, 16, 16, 2048, 64, True, 1.0),
+    "C2": (1, 8, 8, 4096, 128, True, 1.0),
+    "C3a": (4, 32, 8, 3000, 128, False, 0.5),
+    "C3b": (2, 16, 1, 1537, 64, False, 0.5),
+    "north_star": (1, 32, 32, 8192, 128, True, 1.0),
+}
+FALLBACK_PEAK_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def flops_fwd(B, Hq, N, D, causal):
+    pairs = N * (N + 1) / 2 if causal else float(N) * N
+    return 4.0 * B * Hq * D * pairs
+
+
+def load_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["bf16_tflops"]), float(pk["hbm_gbs"]), "measured (MEASURED_PEAKS.json, burst)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_PEAK_TFLOPS, 6650.0, "fallback"
+
+
+def load_traffic(workload):
+    """dram bytes per launch of each kernel, from a committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload, {})
+    except (OSError, ValueError):
+        return {}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML while running."""
+
+    REASONS = {
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_indices, period_s=0.01):
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in device_indices]
+            self.max_mhz = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                               for h in self._handles)
+        except Exception:  # NVML unavailable: report no clock data
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            for h in self._handles:
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    util = nv.nvmlDeviceGetUtilizationRates(h).gpu
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((mhz, util, reasons))
+                except Exception:
+                    pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0, "source": "nvml unavailable"}
+        loaded = [s for s in self.samples if s[1] > 0] or self.samples
+        reasons = set()
+        for _, _, r in loaded:
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[0] for s in loaded), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples),
+                "samples_under_load": len(loaded), "source": "nvml"}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's path on the host cores (bounded sample)
+# ---------------------------------------------------------------------------
+def cpu_sample_shape(workload):
+    """One (batch, kv-group) slice of the workload: the GQA group of query heads
+    that share kv head 0, at the full sequence length."""
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[workload]
+    return 1, Hq // Hkv, 1, N, D, causal, sc
+
+
+def cpu_step_tflops(workload, steps, warmup, min_seconds=0.0):
+    """Median TFLOPS of the CPU reference step over `steps` timed calls (more
+    calls, up to 200, until `min_seconds` of CPU work have been timed)."""
+    from oracle import attention_oracle as orc
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, Hq, Hkv, N, D, causal, sc = cpu_sample_shape(workload)
+    q, k, v, do = orc.seeded_inputs(B, Hq, Hkv, N, D, seed=7, scale=sc)
+    for _ in range(warmup):
+        orc.reference_step(q, k, v, do, causal)
+    times = []
+    while len(times) < steps or (sum(times) < min_seconds and len(times) < 200):
+        t0 = time.perf_counter()
+        orc.reference_step(q, k, v, do, causal)
+        times.append(time.perf_counter() - t0)
+    fl = 3.5 * flops_fwd(B, Hq, N, D, causal)
+    ms = statistics.median(times) * 1e3
+    sample = (f"{B}x{Hq}q/{Hkv}kv heads of {workload}, N={N}, D={D}, causal={causal}: "
+              f"torch fp32 eager fwd+bwd (fa_p100.reference formula) on the host")
+    return fl / (ms * 1e-3) / 1e12, ms, torch.get_num_threads(), sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    value, ms, cores, sample = cpu_step_tflops(args.workload, args.steps, args.warmup)
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS[args.workload]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
+                   "causal": causal, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU side: our kernels
+# ---------------------------------------------------------------------------
+STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ = 1, 2, 4
+KERNELS = ("fwd", "bwd_rowsum", "bwd_dkdv", "bwd_dq")
+
+
+def kernel_work(name, B, Hq, Hkv, N, D, causal):
+    """Algorithmic work of one launch: (amount, unit, bound).
+    fwd: the forward's 2 contractions; dkdv: 4 of the backward's 5 (S recompute,
+    dP, dV, dK); dq: the dQ contraction only (its S/dP recompute is not counted);
+    rowsum: bytes of O and dO read plus Dv written."""
+    ff = flops_fwd(B, Hq, N, D, causal)
+    if name == "fwd":
+        return ff, "TFLOP/s", "tensor"
+    if name == "bwd_dkdv":
+        return 2.0 * ff, "TFLOP/s", "tensor"
+    if name == "bwd_dq":
+        return 0.5 * ff, "TFLOP/s", "tensor"
+    return 2.0 * B * Hq * N * D * 2 + B * Hq * N * 4, "GB/s", "hbm"
+
+
+def run_ours(args, world, rank, local):
+    import _lib
+    import fa_p100
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = _lib.lib()
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[args.workload]
+    gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
+
+    def rnd(h):
+        return (torch.randn(B, h, N, D, generator=gen) * sc).half()
+
+    q_h, k_h, v_h, do_h = rnd(Hq), rnd(Hkv), rnd(Hkv), rnd(Hq)
+    q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, N, device=dev)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, Hq, N)
+    ws = torch.empty(ws_bytes // 4, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    ev = {n: [] for n in KERNELS}
+    step_ev = []
+
+    def bwd_stage(mask):
+        return lib.fa_b200_backward_stages(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), o.data_ptr(),
+            lse.data_ptr(), dq.data_ptr(), 0, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
+            ws_bytes, B, Hq, Hkv, N, D, int(causal), mask, sp)
+
+    def step(record):
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        if record:
+            marks[0].record(stream)
+        st = lib.fa_b200_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                 lse.data_ptr(), B, Hq, Hkv, N, D, int(causal), 0, sp)
+        _lib.check(st, "fa_b200_forward")
+        for i, mask in enumerate((STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ)):
+            if record:
+                marks[i + 1].record(stream)
+            _lib.check(bwd_stage(mask), "fa_b200_backward_stages")
+        if record:
+            marks[4].record(stream)
+            step_ev.append(marks)
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        step(False)
+    torch.cuda.synchronize(dev)
+    if _lib.device_error(local) != 0:
+        raise RuntimeError("device error word set during warm-up")
+
+    devices = [local]
+    with ClockSampler(devices) as clocks:
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        for _ in range(args.steps):
+            flush.fill_(1.0)   # L2 flush, outside the step's events
+            step(True)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    launches = 4 * args.steps
+
+    per_kernel = {n: 0.0 for n in KERNELS}
+    total_ms = 0.0
+    for m in step_ev:
+        for i, n in enumerate(KERNELS):
+            per_kernel[n] += m[i].elapsed_time(m[i + 1])
+        total_ms += m[0].elapsed_time(m[4])
+    ms = total_ms / args.steps
+    ms = max_over_ranks(ms, world, dev)
+    per_kernel = {n: t / args.steps for n, t in per_kernel.items()}
+
+    # e2e: public API, host buffers, copies inside the timed region
+    pin = [t.pin_memory() for t in (q_h, k_h, v_h, do_h)]
+    outs_h = [torch.empty(t.shape, dtype=torch.float16).pin_memory() for t in (q_h, k_h, v_h)]
+    dq_d = torch.empty_like(q)
+
+    def e2e_step():
+        qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in pin)
+        for t in (qd, kd, vd):
+            t.requires_grad_(True)
+        out = fa_p100.flash_attn(qd, kd, vd, causal)
+        out.backward(dod)
+        for h, t in zip(outs_h, (qd.grad, kd.grad, vd.grad)):
+            h.copy_(t, non_blocking=True)
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = 0.0
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_step()
+        b.record(stream)
+        b.synchronize()
+        e2e_ms += a.elapsed_time(b)
+    barrier(world)
+    launches += 4 * args.steps
+    e2e_ms = max_over_ranks(e2e_ms / args.steps, world, dev)
+    del dq_d
+    if _lib.device_error(local) != 0:
+        raise RuntimeError("device error word set during the timed steps")
+
+    step_flops = 3.5 * flops_fwd(B, Hq, N, D, causal)
+    value = world * step_flops / (ms * 1e-3) / 1e12
+    e2e_value = world * step_flops / (e2e_ms * 1e-3) / 1e12
+    peak_tf, peak_gbs, peak_src = load_peak()
+
+    # roofline of the dominant kernel
+    dom = max(per_kernel, key=per_kernel.get)
+    work, unit, bound = kernel_work(dom, B, Hq, Hkv, N, D, causal)
+    t_s = per_kernel[dom] * 1e-3
+    achieved = work / t_s / (1e12 if unit == "TFLOP/s" else 1e9)
+    peak = peak_tf if unit == "TFLOP/s" else peak_gbs
+    traffic = load_traffic(args.workload).get(dom)
+    kernels = {}
+    for n in KERNELS:
+        w, u, _ = kernel_work(n, B, Hq, Hkv, N, D, causal)
+        kernels[n] = {"ms": per_kernel[n],
+                      "achieved": w / (per_kernel[n] * 1e-3) / (1e12 if u == "TFLOP/s" else 1e9),
+                      "unit": u}
+
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+        "pct_of_peak": 100.0 * value / world / peak_tf,
+        "peak_tflops": peak_tf, "peak_source": peak_src,
+        "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
+                   "causal": causal, "inputs": f"N(0,1)*{sc} fp16, seeded",
+                   "l2": "flushed (256 MiB write) between steps, outside the timed events",
+                   "parallelism": f"head-sharded x{world}" if world > 1 else "single GPU",
+                   "flops_per_step_per_gpu": step_flops,
+                   "flop_convention": "fwd 4*B*Hq*D*pairs (causal pairs N(N+1)/2), fwd+bwd 3.5x"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": sum(t.numel() * 2 for t in pin),
+                "d2h_bytes_per_step": sum(t.numel() * 2 for t in outs_h),
+                "path": "fa_p100.flash_attn + autograd backward, pinned host buffers"},
+        "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
+                     "unit": unit, "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": peak_src},
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cpu_tf, _, cores, sample = cpu_step_tflops(args.workload, 3, 1, min_seconds=10.0)
+        line["cpu_baseline"] = {"value": cpu_tf, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": sample}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="C2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, local = dist_setup(args) if args.impl == "ours" else (
+        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_ours(args, world, rank, local)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

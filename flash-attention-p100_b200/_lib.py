@@ -19,6 +19,8 @@ SIGNATURES = {
     "fa_b200_backward_workspace_bytes": (_SZ, [_I, _I, _I]),
     "fa_b200_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                               _I, _I, _I, _I, _I, _I, _P]),
+    "fa_b200_backward_stages": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
+                                     _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_device_error": (_I, [_I, _I]),
     "fa_b200_status_string": (ctypes.c_char_p, [_I]),
     "fa_b200_last_error": (ctypes.c_char_p, []),

@@ -166,7 +166,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
 template <int D>
 int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
                     const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* dvec, int B,
-                    int Hq, int Hkv, int N, int causal, cudaStream_t stream, int* err) {
+                    int Hq, int Hkv, int N, int causal, int stages, cudaStream_t stream, int* err) {
   const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
   const int nq128 = (N + 127) / 128;
   if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
@@ -198,17 +198,24 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
 
-  const long long rows = static_cast<long long>(BH) * N;
-  const long long threads = rows * (D / 8);
-  bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-      static_cast<const __half*>(o), static_cast<const __half*>(dO), dvec, rows);
-  if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
-  bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
-                       DkdvCfg<D>::SMEM, stream>>>(tq64, tk128, tv128, tdo64, p);
-  if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
-  bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
-                     stream>>>(tq128, tk64, tv64, tdo128, p);
-  return cudaGetLastError() == cudaSuccess ? FA_B200_OK : FA_B200_ERR_LAUNCH;
+  if (stages & FA_B200_STAGE_ROWSUM) {
+    const long long rows = static_cast<long long>(BH) * N;
+    const long long threads = rows * (D / 8);
+    bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+        static_cast<const __half*>(o), static_cast<const __half*>(dO), dvec, rows);
+    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  }
+  if (stages & FA_B200_STAGE_DKDV) {
+    bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
+                         DkdvCfg<D>::SMEM, stream>>>(tq64, tk128, tv128, tdo64, p);
+    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  }
+  if (stages & FA_B200_STAGE_DQ) {
+    bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
+                       stream>>>(tq128, tk64, tv64, tdo128, p);
+    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  }
+  return FA_B200_OK;
 }
 
 }  // namespace
@@ -335,6 +342,16 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream) {
+  return fa_b200_backward_stages(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace,
+                                 workspace_bytes, B, Hq, Hkv, N, D, causal, FA_B200_STAGE_ALL,
+                                 stream);
+}
+
+int fa_b200_backward_stages(const void* q, const void* k, const void* v, const void* dO,
+                            const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
+                            void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
+                            int Hkv, int N, int D, int causal, int stages, void* stream) {
+  if (stages & ~FA_B200_STAGE_ALL) return FA_B200_ERR_SHAPE;
   if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
   int st = fab::check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
@@ -350,9 +367,9 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
   auto s = static_cast<cudaStream_t>(stream);
   float* dvec = static_cast<float*>(workspace);
   return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
-                                            Hkv, N, causal, s, err)
+                                            Hkv, N, causal, stages, s, err)
                  : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
-                                             Hkv, N, causal, s, err);
+                                             Hkv, N, causal, stages, s, err);
 }
 
 int fa_b200_device_error(int device, int reset) {

@@ -61,6 +61,24 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream);
 
+/* Stages of the backward, for fa_b200_backward_stages. */
+enum {
+  FA_B200_STAGE_ROWSUM = 1,  /* Dv = rowsum(dO o O) into the workspace */
+  FA_B200_STAGE_DKDV = 2,    /* dK, dV (reads the workspace) */
+  FA_B200_STAGE_DQ = 4,      /* dQ (reads the workspace) */
+  FA_B200_STAGE_ALL = 7
+};
+
+/* fa_b200_backward restricted to the stages in `stages`. The dK/dV and dQ
+ * stages only read the row sums, so once FA_B200_STAGE_ROWSUM has run they may
+ * be enqueued on two streams and overlap. fa_b200_backward(...) is
+ * fa_b200_backward_stages(..., FA_B200_STAGE_ALL, stream). No counterpart in
+ * the reference, whose backward is one launcher (flash_bwd.cuh:466-484). */
+int fa_b200_backward_stages(const void* q, const void* k, const void* v, const void* dO,
+                            const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
+                            void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
+                            int Hkv, int N, int D, int causal, int stages, void* stream);
+
 /* Reads the device error word the kernels set when a bounded internal wait
  * gives up (1..4; 0 = none) on `device`, and clears it when `reset` != 0.
  * Synchronises that device. Returns -1 if the read itself fails. Has no

@@ -132,3 +132,21 @@ def flops_fwd(B, Hq, N, D, causal):
 
 def to_numpy(t):
     return np.ascontiguousarray(torch.as_tensor(t).detach().cpu().numpy())
+
+
+def reference_step(q, k, v, do, causal=False):
+    """One fwd+bwd of the reference's CPU path, timed as the CPU baseline:
+    fa_p100.reference's formula (fa_p100.py:65-75) in fp32 on the host, with
+    the gradients taken by autograd as the reference's tests take them
+    (test_fa_p100.py:90-96). Returns (O, dQ, dK, dV)."""
+    qf, kf, vf = (t.detach().to("cpu", torch.float32).requires_grad_(True) for t in (q, k, v))
+    g = _group(qf, kf)
+    ke = kf.repeat_interleave(g, dim=1) if g > 1 else kf
+    ve = vf.repeat_interleave(g, dim=1) if g > 1 else vf
+    s = (qf @ ke.transpose(-1, -2)) * (1.0 / math.sqrt(qf.shape[-1]))
+    if causal:
+        n = qf.shape[-2]
+        s = s.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+    o = torch.softmax(s, dim=-1) @ ve
+    o.backward(do.detach().to("cpu", torch.float32))
+    return o.detach(), qf.grad, kf.grad, vf.grad
