@@ -21,6 +21,9 @@ SIGNATURES = {
                               _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_stages": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                                      _I, _I, _I, _I, _I, _I, _I, _P]),
+    "fa_b200_backward_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P,
+                                      _I, _I, _I, _I, _I, _I, _P]),
+    "fa_b200_backward_noalloc_max_rows": (_SZ, []),
     "fa_b200_device_error": (_I, [_I, _I]),
     "fa_b200_status_string": (ctypes.c_char_p, [_I]),
     "fa_b200_last_error": (ctypes.c_char_p, []),

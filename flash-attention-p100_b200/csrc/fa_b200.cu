@@ -26,6 +26,14 @@ namespace fab {
 // Device error word: set by a kernel whose bounded wait gave up.
 __device__ int g_device_error;
 
+// Scratch for fa_b200_backward_noalloc: the Dv row sums (one fp32 per query
+// row, B*Hq*N of them) live here instead of in caller-provided memory. It is a
+// fixed 16 MiB on every GPU that loads this library, for as long as the process
+// lives. Host code cannot use the symbol's name as a device address; the
+// address is fetched once per device with cudaGetSymbolAddress.
+constexpr size_t kNoAllocRows = size_t(1) << 22;  // 4,194,304 rows = 16 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocRows];
+
 namespace {
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -43,6 +51,7 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
+float* g_noalloc_ptr[kMaxDevices] = {};  // device address of g_noalloc_scratch
 EncodeTiledFn g_encode = nullptr;
 
 // Detail of the most recent failure on this host thread (fa_b200_last_error).
@@ -130,6 +139,22 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Device address of g_noalloc_scratch on `dev`, looked up once per device with
+// that device current (device_setup has just made it current on this thread).
+float* noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_noalloc_ptr[dev]) {
+    float* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+      set_last_error("cudaGetSymbolAddress(g_noalloc_scratch) failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  return g_noalloc_ptr[dev];
+}
 
 int check_shape(int B, int Hq, int Hkv, int N, int D) {
   if (D != 64 && D != 128) return FA_B200_ERR_HEAD_DIM;
@@ -372,6 +397,39 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
                                              Hkv, N, causal, stages, s, err);
 }
 
+size_t fa_b200_backward_noalloc_max_rows(void) { return fab::kNoAllocRows; }
+
+int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const void* dO,
+                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
+                             void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
+                             void* stream) {
+  if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
+  int st = fab::check_shape(B, Hq, Hkv, N, D);
+  if (st != FA_B200_OK) return st;
+  const size_t rows = static_cast<size_t>(B) * Hq * N;
+  if (rows > fab::kNoAllocRows) {
+    fab::set_last_error(
+        "fa_b200_backward_noalloc: B*Hq*N = %zu query rows exceeds the built-in scratch of %zu "
+        "rows (16 MiB); call fa_b200_backward with a caller-allocated workspace instead",
+        rows, fab::kNoAllocRows);
+    return FA_B200_ERR_SCRATCH_LIMIT;
+  }
+  const void* ptrs[] = {q, k, v, dO, o, lse, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    if (!fab::aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
+  int dev = 0;
+  int* err = nullptr;
+  st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  float* dvec = fab::noalloc_scratch(dev);
+  if (!dvec) return FA_B200_ERR_DEVICE;
+  auto s = static_cast<cudaStream_t>(stream);
+  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                                            Hkv, N, causal, FA_B200_STAGE_ALL, s, err)
+                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                                             Hkv, N, causal, FA_B200_STAGE_ALL, s, err);
+}
+
 int fa_b200_device_error(int device, int reset) {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return -1;
@@ -400,6 +458,7 @@ const char* fa_b200_status_string(int status) {
     case FA_B200_ERR_WORKSPACE: return "workspace missing or too small";
     case FA_B200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FA_B200_ERR_TOO_LARGE: return "problem exceeds a CUDA grid limit";
+    case FA_B200_ERR_SCRATCH_LIMIT: return "problem exceeds the built-in scratch of the no-allocation backward";
     default: return "unknown status";
   }
 }

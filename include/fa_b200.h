@@ -36,7 +36,8 @@ enum {
   FA_B200_ERR_LAUNCH = 6,          /* a kernel launch failed (cudaGetLastError) */
   FA_B200_ERR_WORKSPACE = 7,       /* workspace missing or smaller than required */
   FA_B200_ERR_DEVICE = 8,          /* current device is not compute capability 10.x */
-  FA_B200_ERR_TOO_LARGE = 9        /* a grid dimension would exceed CUDA limits */
+  FA_B200_ERR_TOO_LARGE = 9,       /* a grid dimension would exceed CUDA limits */
+  FA_B200_ERR_SCRATCH_LIMIT = 10   /* B*Hq*N above fa_b200_backward_noalloc_max_rows() */
 };
 
 /* Forward. Replaces fa_forward (reference fa_p100_ext.cu:53-83) and
@@ -78,6 +79,30 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
                             int Hkv, int N, int D, int causal, int stages, void* stream);
+
+/* Backward that allocates nothing and takes no workspace. No counterpart in
+ * the reference. For callers that cannot hand the library device memory of
+ * its own: a host whose device memory is owned entirely by another allocator
+ * (a framework's caching pool, an engine that only passes its plugins the
+ * tensors of the op) or a serving loop that must not call cudaMalloc, whose
+ * implicit synchronisation would stall every stream on the device.
+ * Same inputs, outputs and results as fa_b200_backward; the Dv row sums go to
+ * a 16 MiB array compiled into the library (resident on every GPU that loads
+ * it until the process exits), so B*Hq*N may be at most
+ * fa_b200_backward_noalloc_max_rows() = 4,194,304 (FA_B200_ERR_SCRATCH_LIMIT
+ * otherwise). The first call on a device looks up that array's device address
+ * (and does the library's one-time device set-up); make that first call before
+ * any stream capture. Every call on a device shares the one array: calls whose
+ * backward passes overlap on the GPU (different streams, or different host
+ * threads) race on it and must be serialised by the caller. Nothing in it has
+ * to start at zero: each call writes every row sum it reads. */
+int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const void* dO,
+                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
+                             void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
+                             void* stream);
+
+/* Largest B*Hq*N fa_b200_backward_noalloc accepts. */
+size_t fa_b200_backward_noalloc_max_rows(void);
 
 /* Reads the device error word the kernels set when a bounded internal wait
  * gives up (1..4; 0 = none) on `device`, and clears it when `reset` != 0.
