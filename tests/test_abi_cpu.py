@@ -1,0 +1,94 @@
+"""The C ABI without a GPU: the library loads, exports every function
+include/fa_b200.h declares, and rejects bad arguments with the documented status
+codes before touching a device (so nothing here launches or needs CUDA)."""
+import os
+import re
+
+import pytest
+
+import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "fa_b200.h")
+P = 4096          # a 16-byte aligned fake device address, never dereferenced
+MISALIGNED = 4097
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(fa_b200_\w+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    names = declared()
+    assert len(names) >= 9
+    lib = _lib.lib()
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in fa_b200.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def fwd(q=P, k=P, v=P, o=P, lse=P, B=1, Hq=4, Hkv=2, N=16, D=64):
+    return _lib.lib().fa_b200_forward(q, k, v, o, lse, B, Hq, Hkv, N, D, 1, 0, None)
+
+
+def test_forward_argument_errors():
+    assert fwd(q=None) == 1
+    assert fwd(lse=None) == 1
+    assert fwd(D=96) == 2
+    assert fwd(D=256) == 2
+    assert fwd(N=0) == 3
+    assert fwd(Hq=6, Hkv=4) == 3
+    assert fwd(Hkv=0) == 3
+    assert fwd(B=0) == 3
+    assert fwd(o=MISALIGNED) == 4
+
+
+def bwd(ws=P, ws_bytes=1 << 20, stages=None, **kw):
+    a = dict(B=1, Hq=4, Hkv=2, N=16, D=64)
+    a.update(kw)
+    lib = _lib.lib()
+    args = [P, P, P, P, P, P, P, 1, P, P, ws, ws_bytes, a["B"], a["Hq"], a["Hkv"], a["N"],
+            a["D"], 1]
+    if stages is None:
+        return lib.fa_b200_backward(*args, None)
+    return lib.fa_b200_backward_stages(*args, stages, None)
+
+
+def test_backward_argument_errors():
+    assert bwd(D=80) == 2
+    assert bwd(Hq=3, Hkv=2) == 3
+    assert bwd(ws=None) == 7
+    assert bwd(ws_bytes=4 * 4 * 16 - 4) == 7       # one float short of B*Hq*N
+    assert bwd(ws=MISALIGNED) == 4
+    assert bwd(stages=8) == 3                       # unknown stage bit
+
+
+def test_workspace_size():
+    lib = _lib.lib()
+    assert lib.fa_b200_backward_workspace_bytes(2, 8, 100) == 6400   # 2*8*100*4, 256-aligned
+    assert lib.fa_b200_backward_workspace_bytes(1, 1, 1) == 256
+    assert lib.fa_b200_backward_workspace_bytes(0, 1, 1) == 0
+
+
+def test_noalloc_limit_and_errors():
+    lib = _lib.lib()
+    rows = lib.fa_b200_backward_noalloc_max_rows()
+    assert rows == 1 << 22
+    st = lib.fa_b200_backward_noalloc(P, P, P, P, P, P, P, 1, P, P, 1, 32, 32, rows // 32 + 1,
+                                      64, 1, None)
+    assert st == 10
+    assert "exceeds the built-in scratch" in lib.fa_b200_last_error().decode()
+    assert lib.fa_b200_backward_noalloc(None, P, P, P, P, P, P, 1, P, P, 1, 1, 1, 8, 64, 0,
+                                        None) == 1
+
+
+def test_selftest_rejects_unsupported_mode():
+    assert _lib.lib().fa_b200_selftest_gemm(P, P, P, 1, 0, 1, None) == 3
+
+
+@pytest.mark.parametrize("code", range(0, 11))
+def test_status_strings(code):
+    text = _lib.status_string(code)
+    assert text and text != "unknown status"
+    assert _lib.status_string(99) == "unknown status"
