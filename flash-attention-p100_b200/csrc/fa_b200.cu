@@ -26,13 +26,14 @@ namespace fab {
 // Device error word: set by a kernel whose bounded wait gave up.
 __device__ int g_device_error;
 
-// Scratch for fa_b200_backward_noalloc: the Dv row sums (one fp32 per query
-// row, B*Hq*N of them) live here instead of in caller-provided memory. It is a
-// fixed 16 MiB on every GPU that loads this library, for as long as the process
-// lives. Host code cannot use the symbol's name as a device address; the
-// address is fetched once per device with cudaGetSymbolAddress.
-constexpr size_t kNoAllocRows = size_t(1) << 22;  // 4,194,304 rows = 16 MiB
-static __device__ __align__(256) float g_noalloc_scratch[kNoAllocRows];
+// Scratch for fa_b200_backward_noalloc: the backward's per-row workspace (Dv
+// and LSE*log2e, two floats per padded query row, B*Hq*roundup(N,128) rows)
+// lives here instead of in caller-provided memory. It is a fixed 16 MiB on every
+// GPU that loads this library, for as long as the process lives. Host code
+// cannot use the symbol's name as a device address; the address is fetched
+// once per device with cudaGetSymbolAddress.
+constexpr size_t kNoAllocRows = size_t(1) << 21;  // 2,097,152 padded rows x 8 B = 16 MiB
+static __device__ __align__(256) float g_noalloc_scratch[2 * kNoAllocRows];
 
 namespace {
 
@@ -190,27 +191,27 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
 
 template <int D>
 int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
-                    const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* dvec, int B,
+                    const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* ws, int B,
                     int Hq, int Hkv, int N, int causal, int stages, cudaStream_t stream, int* err) {
   const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
   const int nq128 = (N + 127) / 128;
   if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-  // Q/dO boxes are 64 rows for the key-stationary kernel, 128 for the dQ kernel.
-  CUtensorMap tq64, tdo64, tk128, tv128, tq128, tdo128, tk64, tv64;
-  if (!make_map(&tq64, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 64) ||
-      !make_map(&tdo64, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 64) ||
-      !make_map(&tk128, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
-      !make_map(&tv128, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
-      !make_map(&tq128, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
-      !make_map(&tdo128, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
-      !make_map(&tk64, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 64) ||
-      !make_map(&tv64, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 64))
+  // Every operand tile of both gradient kernels is 128 rows.
+  CUtensorMap tq, tdo, tk, tv;
+  if (!make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
+      !make_map(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
+      !make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
+      !make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128))
     return FA_B200_ERR_TENSOR_MAP;
   BwdParams p;
   p.o = static_cast<const __half*>(o);
   p.dO = static_cast<const __half*>(dO);
   p.lse = lse;
-  p.dvec = dvec;
+  const int n_pad = pad_rows(N);
+  const long long rows_pad = static_cast<long long>(BH) * n_pad;
+  p.dvec = ws;
+  p.lse2 = ws + rows_pad;
+  p.n_pad = n_pad;
   p.dq = dq;
   p.dk = static_cast<__half*>(dk);
   p.dv = static_cast<__half*>(dv);
@@ -224,20 +225,20 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
 
   if (stages & FA_B200_STAGE_ROWSUM) {
-    const long long rows = static_cast<long long>(BH) * N;
-    const long long threads = rows * (D / 8);
+    const long long threads = rows_pad * (D / 8);
     bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const __half*>(o), static_cast<const __half*>(dO), dvec, rows);
+        static_cast<const __half*>(o), static_cast<const __half*>(dO), lse, p.dvec, p.lse2, N,
+        n_pad, rows_pad, p.scale);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_DKDV) {
     bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
-                         DkdvCfg<D>::SMEM, stream>>>(tq64, tk128, tv128, tdo64, p);
+                         DkdvCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_DQ) {
     bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
-                       stream>>>(tq128, tk64, tv64, tdo128, p);
+                       stream>>>(tq, tk, tv, tdo, p);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   return FA_B200_OK;
@@ -270,8 +271,8 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) tmem_alloc(smem_u32(tmem_slot), 128);
-  if (a_by_threads && threadIdx.x < 128) {
+  if (warp == 4) tmem_alloc(smem_u32(tmem_slot), 256);
+  if (a_by_threads == 1 && threadIdx.x < 128) {
     // A is [M][K]; thread m writes its row into the swizzled K-major layout.
     const int m = threadIdx.x;
     for (int c8 = 0; c8 < 16; ++c8) {
@@ -284,6 +285,21 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (a_by_threads == 2 && threadIdx.x < 128) {
+    // A is [M][K]; thread m stores its row into TMEM lane m, columns 128..191,
+    // two fp16 per 32-bit column (the A-from-TMEM operand layout).
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    for (int h = 0; h < 2; ++h) {
+      uint32_t v[32];
+      for (int i = 0; i < 32; ++i)
+        v[i] = reinterpret_cast<const uint32_t*>(a_raw + threadIdx.x * 128)[32 * h + i];
+      tmem_st32(tmem + 128 + 32 * h + lane_off, v);
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (threadIdx.x == 160) {
     mbar_arrive_expect_tx(b_ld, a_by_threads ? 32768 : 65536);
     for (int ch = 0; ch < 2; ++ch) {
@@ -301,7 +317,10 @@ __global__ void __launch_bounds__(192, 1)
                                  : sdesc_sw128(s_a + koff, 16, 1024);
         const uint64_t db = b_mn ? sdesc_sw128(s_b + kk * 2048, 16384, 1024)
                                  : sdesc_sw128(s_b + koff, 16, 1024);
-        mma_ss(tmem, da, db, id, kk > 0 ? 1u : 0u);
+        if (a_by_threads == 2)
+          mma_ts(tmem, tmem + 128 + kk * 8, db, id, kk > 0 ? 1u : 0u);
+        else
+          mma_ss(tmem, da, db, id, kk > 0 ? 1u : 0u);
       }
       mma_commit(b_mma);
     } else {
@@ -327,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   if (warp == 4) {
     __syncwarp();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -358,9 +377,9 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
 
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {
   if (B < 1 || Hq < 1 || N < 1) return 0;
-  // rounded up to 256 bytes so a caller can carve further buffers after it
-  const size_t bytes = static_cast<size_t>(B) * Hq * N * sizeof(float);
-  return (bytes + 255) & ~static_cast<size_t>(255);
+  // Dv and LSE*log2e for every query row, each head padded to a multiple of
+  // 128 rows (a multiple of 512 bytes, so the total needs no rounding).
+  return 2 * static_cast<size_t>(B) * Hq * fab::pad_rows(N) * sizeof(float);
 }
 
 int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
@@ -390,10 +409,10 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
   st = fab::device_setup(&dev, &err);
   if (st != FA_B200_OK) return st;
   auto s = static_cast<cudaStream_t>(stream);
-  float* dvec = static_cast<float*>(workspace);
-  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+  float* ws = static_cast<float*>(workspace);
+  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
                                             Hkv, N, causal, stages, s, err)
-                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
                                              Hkv, N, causal, stages, s, err);
 }
 
@@ -406,11 +425,12 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
   if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
   int st = fab::check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
-  const size_t rows = static_cast<size_t>(B) * Hq * N;
+  const size_t rows = static_cast<size_t>(B) * Hq * fab::pad_rows(N);
   if (rows > fab::kNoAllocRows) {
     fab::set_last_error(
-        "fa_b200_backward_noalloc: B*Hq*N = %zu query rows exceeds the built-in scratch of %zu "
-        "rows (16 MiB); call fa_b200_backward with a caller-allocated workspace instead",
+        "fa_b200_backward_noalloc: B*Hq*roundup(N,128) = %zu query rows exceeds the built-in "
+        "scratch of %zu rows (16 MiB); call fa_b200_backward with a caller-allocated workspace "
+        "instead",
         rows, fab::kNoAllocRows);
     return FA_B200_ERR_SCRATCH_LIMIT;
   }
@@ -421,12 +441,12 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
   int* err = nullptr;
   st = fab::device_setup(&dev, &err);
   if (st != FA_B200_OK) return st;
-  float* dvec = fab::noalloc_scratch(dev);
-  if (!dvec) return FA_B200_ERR_DEVICE;
+  float* ws = fab::noalloc_scratch(dev);
+  if (!ws) return FA_B200_ERR_DEVICE;
   auto s = static_cast<cudaStream_t>(stream);
-  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
                                             Hkv, N, causal, FA_B200_STAGE_ALL, s, err)
-                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, dvec, B, Hq,
+                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
                                              Hkv, N, causal, FA_B200_STAGE_ALL, s, err);
 }
 

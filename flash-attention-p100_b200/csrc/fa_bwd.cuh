@@ -12,9 +12,20 @@
 // The reference accumulates dQ with fp32 atomicAdd from every key block
 // (flash_bwd.cuh:442). Here dQ is computed by its own query-stationary kernel
 // that owns each dQ row outright, so there are no global atomics and the
-// result is deterministic. dK/dV come from a key-stationary kernel that loops
+// result is deterministic.
+//
+// Every MMA here has N = 128: a tcgen05.mma with K = 16 costs about the same
+// ~95-110 cycles for N = 64 as for N = 128 (measured on B200), so the query
+// step of the dK/dV kernel and the key step of the dQ kernel are 128 wide. dK/dV come from a key-stationary kernel that loops
 // over the GQA group and all query blocks, keeping both accumulators in TMEM
 // (as the reference keeps them in registers, flash_bwd.cuh:163, :448-463).
+//
+// Workspace (written by the preprocess, read by both gradient kernels): per
+// (batch, q-head) a row of n_pad = roundup(N, 128) floats of Dv * scale, then
+// the same for LSE * log2(e). Padded rows hold 0 and +inf, so P = 0 there
+// without a bounds test, and every 128-row slice starts 512-byte aligned, which
+// lets the TMA warp bulk-copy a query block's slice next to its Q tile. With
+// Dv pre-scaled, dS = scale * P o (dP - Dv) is P * fma(dP, scale, -Dv*scale).
 #pragma once
 #include "sm100.cuh"
 
@@ -24,32 +35,43 @@ struct BwdParams {
   const __half* o;     // (B*Hq, N, D) forward output
   const __half* dO;    // (B*Hq, N, D)
   const float* lse;    // (B*Hq, N) natural log
-  float* dvec;         // (B*Hq, N) workspace: rowsum(dO o O)
+  float* dvec;         // (B*Hq, n_pad) workspace: rowsum(dO o O) * scale
+  float* lse2;         // (B*Hq, n_pad) workspace: LSE * log2(e)
   void* dq;            // (B*Hq, N, D) fp32 or fp16
   __half* dk;          // (B*Hkv, N, D)
   __half* dv;          // (B*Hkv, N, D)
   int* err;
-  int n, hq, group, causal;
+  int n, n_pad, hq, group, causal;
   int dq_fp32;
   float scale;         // 1/sqrt(D)
   float scale_log2;    // scale * log2(e)
 };
 
+__host__ __device__ constexpr int pad_rows(int n) { return (n + 127) / 128 * 128; }
+
 // ---------------------------------------------------------------------------
-// Dv = rowsum(dO o O): HBM-bound, one 16-byte vector per thread, D/8 threads
-// per row reduced with shuffles.
+// Dv * scale = rowsum(dO o O) * scale and LSE * log2(e), over padded rows:
+// HBM-bound, one 16-byte vector per thread, D/8 threads per row reduced with
+// shuffles.
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __restrict__ o,
                                                               const __half* __restrict__ dO,
+                                                              const float* __restrict__ lse,
                                                               float* __restrict__ dvec,
-                                                              long long rows) {
+                                                              float* __restrict__ lse2, int n,
+                                                              int n_pad, long long rows_pad,
+                                                              float scale) {
   constexpr int TPR = D / 8;  // threads per row (8 or 16)
   const long long gtid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long row = gtid / TPR;
+  const long long prow = gtid / TPR;
   const int part = static_cast<int>(gtid % TPR);
+  const long long bh = prow / n_pad;
+  const int r = static_cast<int>(prow - bh * n_pad);
+  const bool real = prow < rows_pad && r < n;
+  const long long row = bh * n + r;
   float acc = 0.f;
-  if (row < rows) {
+  if (real) {
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + row * D) + part);
     const uint4 b = __ldg(reinterpret_cast<const uint4*>(dO + row * D) + part);
     const __half2* ha = reinterpret_cast<const __half2*>(&a);
@@ -64,53 +86,13 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
   }
 #pragma unroll
   for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (row < rows && part == 0) dvec[row] = acc;
+  if (prow < rows_pad && part == 0) {
+    dvec[prow] = real ? acc * scale : 0.f;
+    lse2[prow] = real ? __ldg(lse + row) * 1.4426950408889634f : INFINITY;
+  }
 }
 
-// ---------------------------------------------------------------------------
-// dK / dV: one CTA per (128 keys, batch, kv-head).
-//   warps 0-3  compute: one thread per key row; P^T and dS^T for 64 queries
-//   warp  4    TMEM allocation + MMA issue
-//   warp  5    TMA producer
-// TMEM: S^T[2] cols 0,64 | dP^T[2] cols 128,192 | dV 256..256+D | dK 256+D..
-// Per query block i the MMA thread issues
-//   [P_i] dV += P_i^T dO_i ; S_{i+1} ; dP_{i+1} ; [dS_i] dK += dS_i^T Q_i
-// S^T = K Q^T (A = K, K-major; B = Q, K-major), dP^T = V dO^T (same shapes),
-// dV += P^T dO (A = P^T K-major in smem, B = dO MN-major),
-// dK += dS^T Q  (A = dS^T K-major in smem, B = Q MN-major).
-// dS is stored pre-multiplied by the softmax scale, so dK needs no rescale.
-// ---------------------------------------------------------------------------
-template <int D>
-struct DkdvCfg {
-  static constexpr int BN = 128;  // keys per CTA
-  static constexpr int BM = 64;   // queries per step
-  static constexpr int CH = D / 64;
-  static constexpr int KVBYTES = BN * D * 2;   // K or V tile
-  static constexpr int QBYTES = BM * D * 2;    // Q or dO tile
-  static constexpr int PBYTES = BN * BM * 2;   // P^T or dS^T tile
-  static constexpr int STAGES = (D == 128) ? 6 : 8;
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + KVBYTES;
-  static constexpr int OFF_RING = OFF_V + KVBYTES;
-  static constexpr int OFF_P = OFF_RING + STAGES * QBYTES;
-  static constexpr int OFF_DS = OFF_P + PBYTES;
-  // per compute warp, double-buffered: 64 log2-domain LSE values, 64 Dv values
-  static constexpr int OFF_LSE = OFF_DS + PBYTES;
-  static constexpr int OFF_DV = OFF_LSE + 4 * 2 * BM * 4;
-  static constexpr int OFF_BAR = OFF_DV + 4 * 2 * BM * 4;
-  // kv, full[ST], empty[ST], s[2], dp[2], p, ds, dk, fin
-  static constexpr int NBAR = 1 + 2 * STAGES + 8;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-  static constexpr int THREADS = 192;
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
-};
-
-}  // namespace fab
-
-namespace fab {
-
-// Write one row of 32 fp32 TMEM values as fp16 to global (8 halves per store).
+// Write 32 fp32 values as fp16 / fp32 to global, 16 bytes per store.
 __device__ __forceinline__ void store_row32_f16(__half* dst, const uint32_t (&v)[32], float mul) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -134,38 +116,118 @@ __device__ __forceinline__ void store_row32_f32(float* dst, const uint32_t (&v)[
   }
 }
 
+// Load 32 consecutive TMEM columns of this warp's lanes and wait for them.
+__device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld32(taddr, r);
+  tmem_ld_wait(r);
+}
+
+// Thread-row r writes 32 fp16 values (columns 32*half .. +31 of a 64-column
+// K-major swizzled tile of 128 rows) as four 16-byte pieces.
+__device__ __forceinline__ void st_row32_sw128(uint32_t tile, int r, int half, const float (&x)[32]) {
+#pragma unroll
+  for (int c4 = 0; c4 < 4; ++c4) {
+    const int piece = 4 * half + c4;
+    st_shared_v4(tile + r * 128 + ((piece ^ (r & 7)) << 4), pack_half2(x[8 * c4], x[8 * c4 + 1]),
+                 pack_half2(x[8 * c4 + 2], x[8 * c4 + 3]), pack_half2(x[8 * c4 + 4], x[8 * c4 + 5]),
+                 pack_half2(x[8 * c4 + 6], x[8 * c4 + 7]));
+  }
+}
+
+}  // namespace fab
+
+
+
+namespace fab {
+
+// Store 64 fp32 values as 32 packed fp16 pairs into TMEM columns [col, col+32)
+// of this warp's lanes (the A-operand layout: column c holds elements 2c, 2c+1).
+__device__ __forceinline__ void tmem_st_pairs(uint32_t taddr, const float (&x)[2][32]) {
+  uint32_t v[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const int h = c >> 4, e = 2 * (c & 15);
+    v[c] = pack_half2(x[h][e], x[h][e + 1]);
+  }
+  tmem_st32(taddr, v);
+}
+
+// ---------------------------------------------------------------------------
+// dK / dV: one CTA per (128 keys, batch, kv-head), looping over the GQA group
+// and every query block of 128 at or below the diagonal.
+//   warps 0-7  compute: two warpgroups, one thread per key row each; group w
+//              owns query columns 64w..64w+63 of every 128-query step
+//   warp  8    TMEM allocation + MMA issue
+//   warp  9    TMA producer: K, V once; then Q_i (+ its LSE/Dv slices), dO_i
+// TMEM: S^T cols 0..127 | dP^T 128..255 | dV 256..256+D | dK 256+D..256+2D
+// P^T and dS^T (fp16 pairs) are written by the compute threads into TMEM
+// columns the same threads have already read: P^T over S^T cols 32..95, dS^T
+// over dP^T cols 160..223 (group w writes 32w+32.. / 32w+160.., inside its own
+// 64-column slice), and feed dV += P^T dO and dK += dS^T Q as the A operand
+// from TMEM. MMA order per step i (brackets = what it waits for):
+//   [P_i] dV_i ; [dS_i] dK_i ; [Q_{i+1}] S^T_{i+1} ; [dO_{i+1}] dP^T_{i+1}
+// S^T_{i+1} overwrites P_i and dP^T_{i+1} overwrites dS_i; each is issued
+// after the MMA that reads them, and the tensor core executes one CTA's MMAs
+// in issue order. Q_{i+1} reuses the ring slot Q_{i-1} frees after dK_{i-1},
+// so four MMA groups (~3000 cycles) separate that release from S^T_{i+1}:
+// enough to hide the TMA round trip.
+// Every barrier's arrivals are gated on an MMA that needed all arrivals of the
+// previous phase, so no phase can receive arrivals from two steps.
+// ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+struct DkdvCfg {
+  static constexpr int BN = 128;  // keys per CTA
+  static constexpr int BM = 128;  // queries per step
+  static constexpr int CH = D / 64;
+  static constexpr int TILE = 128 * D * 2;    // K, V, Q or dO tile (128 rows)
+  static constexpr int STAGES = 4;            // ring of Q / dO tiles
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE;
+  static constexpr int OFF_RING = OFF_V + TILE;
+  static constexpr int OFF_LSE = OFF_RING + STAGES * TILE;   // [2][128] LSE*log2e, [2][128] Dv*scale
+  static constexpr int OFF_BAR = OFF_LSE + 2048;
+  // kv, full[ST], empty[ST], s, dp, p, ds, fin
+  static constexpr int NBAR = 1 + 2 * STAGES + 5;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;   // window must start 1024-aligned
+  static constexpr int THREADS = 320;
+  static constexpr int NCOMPUTE = 256;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
+  static constexpr uint32_t COL_P = 32, COL_DS = 160;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const BwdParams p) {
   using C = DkdvCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (!smem_aligned_or_report(smem_raw, p.err)) return;
+  const uint32_t sbase = smem_u32(smem_raw);
   const uint32_t s_k = sbase + C::OFF_K, s_v = sbase + C::OFF_V, s_ring = sbase + C::OFF_RING;
-  const uint32_t s_p = sbase + C::OFF_P, s_ds = sbase + C::OFF_DS;
-  float* lse_s = reinterpret_cast<float*>(sgen + C::OFF_LSE);
-  float* dvec_s = reinterpret_cast<float*>(sgen + C::OFF_DV);
+  const uint32_t s_lse = sbase + C::OFF_LSE;
   const uint32_t b_kv = sbase + C::OFF_BAR;
   const uint32_t b_full = b_kv + 8, b_empty = b_full + 8 * C::STAGES;
-  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 16;
-  const uint32_t b_p = b_dp + 16, b_ds = b_p + 8, b_dk = b_ds + 8, b_fin = b_dk + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
+  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 8, b_p = b_dp + 8, b_ds = b_p + 8,
+                 b_fin = b_ds + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // grid (B*Hkv, key blocks): causal key block 0 has the most work and goes first
-  const int bkv = blockIdx.x;        // b * hkv + kv head
-  const int kvb = blockIdx.y;        // key block
+  const int bkv = blockIdx.x;
+  const int kvb = blockIdx.y;
   const int hkv = p.hq / p.group;
   const int b = bkv / hkv, kvh = bkv % hkv;
   const int kv0 = kvb * C::BN;
   const int nqb = (p.n + C::BM - 1) / C::BM;
-  const int i_start = p.causal ? (kv0 / C::BM) : 0;
+  const int i_start = p.causal ? kvb : 0;   // BM == BN: the diagonal block
   const int nq_head = nqb - i_start;
-  const int total = p.group * nq_head;   // (group head, query block) steps
+  const int total = p.group * nq_head;      // (group head, query block) steps
   const Ctl ctl{abort_flag, p.err};
+  auto slot_of = [](int it) { return it % C::STAGES; };
+  auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
 
   if (threadIdx.x == 0) {
     mbar_init(b_kv, 1);
@@ -173,31 +235,28 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(b_full + 8 * s, 1);
       mbar_init(b_empty + 8 * s, 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(b_s + 8 * t, 1);
-      mbar_init(b_dp + 8 * t, 1);
-    }
-    mbar_init(b_p, 128);
-    mbar_init(b_ds, 128);
-    mbar_init(b_dk, 1);
+    mbar_init(b_s, 1);
+    mbar_init(b_dp, 1);
+    mbar_init(b_p, C::NCOMPUTE);
+    mbar_init(b_ds, C::NCOMPUTE);
     mbar_init(b_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(b_kv, 2 * C::KVBYTES);
+      mbar_arrive_expect_tx(b_kv, 2 * C::TILE);
 #pragma unroll
       for (int c = 0; c < C::CH; ++c) {
         tma_load_3d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, bkv);
@@ -210,17 +269,25 @@ __global__ void __launch_bounds__(192, 1)
         const int q0 = (i_start + step % nq_head) * C::BM;
         const int bh = b * p.hq + kvh * p.group + g;
 #pragma unroll 1
-        for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i then dO_i
-          const int slot = it % C::STAGES;
-          ok = mbar_wait(b_empty + 8 * slot, ((it / C::STAGES) & 1) ^ 1, ctl, kErrTimeoutLoad);
+        for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
+          const int slot = slot_of(it);
+          ok = mbar_wait(b_empty + 8 * slot, ph_of(it) ^ 1, ctl, kErrTimeoutLoad);
           if (!ok) break;
           const uint32_t fb = b_full + 8 * slot;
-          mbar_arrive_expect_tx(fb, C::QBYTES);
-          const uint32_t dst = s_ring + slot * C::QBYTES;
+          const uint32_t dst = s_ring + slot * C::TILE;
+          mbar_arrive_expect_tx(fb, kind ? C::TILE : C::TILE + 1024);
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
-            tma_load_3d(dst + c * (C::BM * 128), kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
+            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
                         c * 64, q0, bh);
+          if (!kind) {
+            // the Q slot of step i is released after dK_i, so slice buffer
+            // i & 1 is free again by the time step i + 2 loads into it
+            const size_t off = static_cast<size_t>(bh) * p.n_pad + q0;
+            const uint32_t ls = s_lse + (step & 1) * 512;
+            bulk_load(ls, p.lse2 + off, 512, fb);
+            bulk_load(ls + 1024, p.dvec + off, 512, fb);
+          }
         }
       }
       if (!ok) {
@@ -228,68 +295,68 @@ __global__ void __launch_bounds__(192, 1)
         drain_loads(b_full, it, C::STAGES);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
-      constexpr uint32_t id_s = idesc_f16(128, C::BM, false, false);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true);       // dV, dK
-      auto slot_of = [](int it) { return it % C::STAGES; };
-      auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
-      // S^T_i = K Q_i^T  /  dP^T_i = V dO_i^T
+      constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV, dK (A from TMEM)
+      // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(d_tmem, sdesc_sw128(a_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                 sdesc_sw128(b_s_ + (kk >> 2) * (C::BM * 128) + (kk & 3) * 32, 16, 1024), id_s,
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_t,
                  kk > 0 ? 1u : 0u);
+        }
       };
-      // acc += X^T_i (128 keys x 64 queries, K-major) * Y_i (64 queries x D, MN-major)
-      auto issue_g = [&](uint32_t d_tmem, uint32_t x_s, uint32_t y_s, bool acc) {
+      // acc += (P or dS)^T (TMEM, 128 keys x 128 queries) * (dO or Q) (MN-major smem)
+      auto issue_g = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t y_s, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < C::BM / 16; ++kk)
-          mma_ss(d_tmem, sdesc_sw128(x_s + kk * 32, 16, 1024),
-                 sdesc_sw128(y_s + kk * 2048, C::BM * 128, 1024), id_g, (acc || kk > 0) ? 1u : 0u);
+          mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(y_s + kk * 2048, 16384, 1024), id_g,
+                 (acc || kk > 0) ? 1u : 0u);
       };
+      auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
-      // prologue: S_0, dP_0
       if (ok) ok = mbar_wait(b_full + 8 * slot_of(0), ph_of(0), ctl, kErrTimeoutMma);
       if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_S, s_k, s_ring + slot_of(0) * C::QBYTES);
+        issue_t(tmem + C::COL_S, s_k, slot_addr(0));
         mma_commit(b_s);
         ok = mbar_wait(b_full + 8 * slot_of(1), ph_of(1), ctl, kErrTimeoutMma);
       }
       if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_DP, s_v, s_ring + slot_of(1) * C::QBYTES);
+        issue_t(tmem + C::COL_DP, s_v, slot_addr(1));
         mma_commit(b_dp);
       }
       for (int i = 0; i < total && ok; ++i) {
         const int it_q = 2 * i, it_do = 2 * i + 1;
+        const bool more = i + 1 < total;
         ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        issue_g(tmem + C::COL_DV, s_p, s_ring + slot_of(it_do) * C::QBYTES, i > 0);
+        issue_g(tmem + C::COL_DV, tmem + C::COL_P, slot_addr(it_do), i > 0);
         mma_commit(b_empty + 8 * slot_of(it_do));
-        if (i + 1 < total) {
-          const int nb = (i + 1) & 1;
-          ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-          issue_t(tmem + C::COL_S + 64 * nb, s_k, s_ring + slot_of(it_q + 2) * C::QBYTES);
-          mma_commit(b_s + 8 * nb);
-          ok = mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-          issue_t(tmem + C::COL_DP + 64 * nb, s_v, s_ring + slot_of(it_do + 2) * C::QBYTES);
-          mma_commit(b_dp + 8 * nb);
-        }
         ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        issue_g(tmem + C::COL_DK, s_ds, s_ring + slot_of(it_q) * C::QBYTES, i > 0);
-        mma_commit(b_dk);
+        issue_g(tmem + C::COL_DK, tmem + C::COL_DS, slot_addr(it_q), i > 0);
         mma_commit(b_empty + 8 * slot_of(it_q));
+        if (more) {
+          ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_S, s_k, slot_addr(it_q + 2));
+          mma_commit(b_s);
+        }
+        if (more) {
+          ok = mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_DP, s_v, slot_addr(it_do + 2));
+          mma_commit(b_dp);
+        }
       }
       mma_commit(b_fin);
       const uint64_t t0 = globaltimer_ns();
@@ -297,117 +364,110 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ compute (warps 0-3)
-    const int r = threadIdx.x;  // key row within the block
+    // ------------------------------------------------------------ compute (warps 0-7)
+    const int w = warp >> 2;            // query half of each step
+    const int r = threadIdx.x & 127;    // key row within the block
     const int kvrow = kv0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qlim = p.causal ? kvrow : -1;  // a query column is live iff qlim <= q < N
     bool ok = true;
     for (int i = 0; i < total; ++i) {
-      const int g = i / nq_head;
-      const int q0 = (i_start + i % nq_head) * C::BM;
-      const int bh = b * p.hq + kvh * p.group + g;
-      const int buf = i & 1;
-      // Each warp stages its own copy of this step's 64 LSE / Dv values, so
-      // the only synchronisation is within the warp (a failed wait in one
-      // warp can never leave another stuck at a barrier).
-      float* lse2w = lse_s + (warp * 2 + buf) * C::BM;
-      float* dvw = dvec_s + (warp * 2 + buf) * C::BM;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int q = q0 + lane + 32 * h;
-        const bool in = q < p.n;
-        lse2w[lane + 32 * h] =
-            in ? p.lse[static_cast<size_t>(bh) * p.n + q] * 1.4426950408889634f : INFINITY;
-        dvw[lane + 32 * h] = in ? p.dvec[static_cast<size_t>(bh) * p.n + q] : 0.f;
-      }
-      __syncwarp();
-      const float* lse2 = lse2w;
-      const float* dv_s = dvw;
-
-      ok = mbar_wait(b_s + 8 * buf, (i >> 1) & 1, ctl, kErrTimeoutSoftmax);
+      const int q0 = (i_start + i % nq_head) * C::BM + 64 * w;
+      const int it_q = 2 * i;
+      const uint32_t ph = i & 1;
+      // one test for the whole CTA: is any (key, query) pair of this half-step masked?
+      const bool need_mask = (q0 + 64 > p.n) || (p.causal && q0 < kv0 + 127);
+      // LSE/Dv slices come with Q_i: wait for that load so they are visible here
+      ok = mbar_wait(b_full + 8 * slot_of(it_q), ph_of(it_q), ctl, kErrTimeoutSoftmax) &&
+           mbar_wait(b_s, ph, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t sr[2][32];
-      tmem_ld32(tmem + C::COL_S + 64 * buf + lane_off, sr[0]);
-      tmem_ld32(tmem + C::COL_S + 64 * buf + 32 + lane_off, sr[1]);
+      tmem_ld32(tmem + C::COL_S + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_S + 64 * w + 32 + lane_off, sr[1]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int k = 0; k < 32; ++k) asm volatile("" : "+r"(sr[c][k]));
-      float pv[64];
-      // keys of a causal step at or below the diagonal keep P; the rest is exactly 0
-      const int qlim = p.causal ? kvrow : -1;  // valid iff q >= qlim
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      // this step's 64 LSE / Dv values for the group, read as 16-byte vectors
+      // (a broadcast LDS per value would cost 8 warps x 64 issue slots on the
+      // shared-memory pipe per phase)
+      const float4* lse4 =
+          reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4;
+      const float4* dvs4 = lse4 + 64;
+      float pv[2][32];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float s = __uint_as_float(sr[c >> 5][c & 31]);
-        const float e = ex2(fmaf(s, p.scale_log2, -lse2[c]));
-        pv[c] = (q0 + c >= qlim) ? e : 0.f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l4 = lse4[8 * h + c4];
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int c = 4 * c4 + e4;
+            pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lv[e4]));
+          }
+        }
+      // Masking is a separate pass, taken only by the steps that need it (the
+      // diagonal block and the ragged tail): a select folded into every
+      // element cost more than the exponentials.
+      if (need_mask) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int q = q0 + 32 * h + c;
+            if (q < qlim || q >= p.n) pv[h][c] = 0.f;
+          }
       }
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        st_shared_v4(s_p + r * 128 + ((c8 ^ (r & 7)) << 4), pack_half2(pv[8 * c8], pv[8 * c8 + 1]),
-                     pack_half2(pv[8 * c8 + 2], pv[8 * c8 + 3]),
-                     pack_half2(pv[8 * c8 + 4], pv[8 * c8 + 5]),
-                     pack_half2(pv[8 * c8 + 6], pv[8 * c8 + 7]));
-      fence_async_smem();
+      tmem_st_pairs(tmem + C::COL_P + 32 * w + lane_off, pv);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p);
 
-      ok = mbar_wait(b_dp + 8 * buf, (i >> 1) & 1, ctl, kErrTimeoutSoftmax);
+      ok = mbar_wait(b_dp, ph, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      tmem_ld32(tmem + C::COL_DP + 64 * buf + lane_off, sr[0]);
-      tmem_ld32(tmem + C::COL_DP + 64 * buf + 32 + lane_off, sr[1]);
+      tmem_ld32(tmem + C::COL_DP + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_DP + 64 * w + 32 + lane_off, sr[1]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int k = 0; k < 32; ++k) asm volatile("" : "+r"(sr[c][k]));
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
 #pragma unroll
-      for (int c = 0; c < 64; ++c)
-        pv[c] = pv[c] * (__uint_as_float(sr[c >> 5][c & 31]) - dv_s[c]) * p.scale;
-      if (i > 0) {
-        ok = mbar_wait(b_dk, (i - 1) & 1, ctl, kErrTimeoutSoftmax);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        st_shared_v4(s_ds + r * 128 + ((c8 ^ (r & 7)) << 4), pack_half2(pv[8 * c8], pv[8 * c8 + 1]),
-                     pack_half2(pv[8 * c8 + 2], pv[8 * c8 + 3]),
-                     pack_half2(pv[8 * c8 + 4], pv[8 * c8 + 5]),
-                     pack_half2(pv[8 * c8 + 6], pv[8 * c8 + 7]));
-      fence_async_smem();
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 d4 = dvs4[8 * h + c4];
+          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4)
+            pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, -dv[e4]);
+        }
+      tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_ds);
     }
-    if (ok) {
+    if (ok && total > 0) {
       ok = mbar_wait(b_fin, 0, ctl, kErrTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      const size_t rowoff = (static_cast<size_t>(bkv) * p.n + kvrow) * D;
+      if (ok) {
+        tc_fence_after();
+        const size_t rowoff = (static_cast<size_t>(bkv) * p.n + kvrow) * D;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + C::COL_DV + 32 * c + lane_off, v);
-        tmem_ld_wait(v);
-        if (total == 0) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = 0u;
+        for (int c = 0; c < D / 64; ++c) {
+          const int col = w * (D / 2) + 32 * c;
+          uint32_t v[32];
+          tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
+          if (kvrow < p.n) store_row32_f16(p.dv + rowoff + col, v, 1.f);
+          tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
+          if (kvrow < p.n) store_row32_f16(p.dk + rowoff + col, v, 1.f);
         }
-        if (kvrow < p.n) store_row32_f16(p.dv + rowoff + 32 * c, v, 1.f);
-        tmem_ld32(tmem + C::COL_DK + 32 * c + lane_off, v);
-        tmem_ld_wait(v);
-        if (total == 0) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = 0u;
-        }
-        if (kvrow < p.n) store_row32_f16(p.dk + rowoff + 32 * c, v, 1.f);
       }
     }
   }
@@ -415,7 +475,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) {
+  if (warp == 8) {
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -426,56 +486,62 @@ __global__ void __launch_bounds__(192, 1)
 namespace fab {
 
 // ---------------------------------------------------------------------------
-// dQ: one CTA per (128 queries, batch*q-head); loops over key blocks of 64.
-//   warps 0-3  compute: one thread per query row; dS for 64 keys
-//   warp  4    TMEM allocation + MMA issue
-//   warp  5    TMA producer (K_j, V_j alternate in one ring)
-// TMEM: S[2] cols 0,64 | dP[2] cols 128,192 | dQ 256..256+D
-// MMA order: S_0 dP_0 S_1 dP_1 [dS_0] dQ+=dS_0 K_0  S_2 dP_2 [dS_1] dQ+=dS_1 K_1 ...
-// S = Q K^T (A = Q K-major, B = K K-major), dP = dO V^T (same shapes),
-// dQ += dS K (A = dS K-major in smem, B = K MN-major).
+// dQ: one CTA per (128 queries, batch*q-head); loops over key blocks of 128.
+//   warps 0-7  compute: two warpgroups, one thread per query row each; group w
+//              owns key columns 64w..64w+63 of every 128-key step
+//   warp  8    TMEM allocation + MMA issue
+//   warp  9    TMA producer: Q, dO once; K_j, V_j alternate in a 4-slot ring
+//   K_j sits in a 3-slot ring (held from S_j until dQ_j) and V_j in a 2-slot
+//   ring (held only for dP_j), so both are loaded well before they are needed
+// TMEM: S cols 0..127 | dP 128..255 | dQ 256..256+D | dS[2] (fp16 pairs) at
+//       384 and 448, 64 columns each
+// MMA order: S_0 dP_0 | per step j: [S_j read] S_{j+1}, [dP_j read] dP_{j+1},
+//            [dS_j] dQ += dS_j K_j
+// S = Q K^T, dP = dO V^T (A, B K-major in smem); dQ += dS K takes A = dS from
+// TMEM (written by the compute threads with tcgen05.st, one query row per
+// lane) and B = K MN-major, so dS never touches shared memory.
+// dS_{j+1} may overwrite buffer (j+1)&1 once dQ_{j-1} is done, which dP_{j+1}
+// being done implies (dP_{j+1} is issued after dQ_{j-1}). dS-ready has one
+// barrier per buffer: a warp can be a full step ahead of another there.
 // ---------------------------------------------------------------------------
 template <int D>
 struct DqCfg {
   static constexpr int BM = 128;  // queries per CTA
-  static constexpr int BN = 64;   // keys per step
+  static constexpr int BN = 128;  // keys per step
   static constexpr int CH = D / 64;
-  static constexpr int QBYTES = BM * D * 2;
-  static constexpr int KVBYTES = BN * D * 2;
-  static constexpr int DSBYTES = BM * BN * 2;
-  static constexpr int STAGES = (D == 128) ? 6 : 8;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int KST = 3, VST = 2;   // K ring, V ring
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_DO = OFF_Q + QBYTES;
-  static constexpr int OFF_RING = OFF_DO + QBYTES;
-  static constexpr int OFF_DS = OFF_RING + STAGES * KVBYTES;
-  static constexpr int OFF_BAR = OFF_DS + 2 * DSBYTES;
-  // qdo, full[ST], empty[ST], s[2], dp[2], ds[2], fin
-  static constexpr int NBAR = 1 + 2 * STAGES + 7;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-  static constexpr int THREADS = 192;
+  static constexpr int OFF_DO = OFF_Q + TILE;
+  static constexpr int OFF_K = OFF_DO + TILE;
+  static constexpr int OFF_V = OFF_K + KST * TILE;
+  static constexpr int OFF_BAR = OFF_V + VST * TILE;
+  // qdo, kfull[3], kempty[3], vfull[2], vempty[2], s, dp, s_free, dp_free, ds[2], fin
+  static constexpr int NBAR = 1 + 2 * KST + 2 * VST + 7;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
+  static constexpr int THREADS = 320;
+  static constexpr int NCOMPUTE = 256;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256;
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256, COL_DS = 384;
 };
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                   const BwdParams p) {
   using C = DqCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-  const uint32_t s_q = sbase + C::OFF_Q, s_do = sbase + C::OFF_DO, s_ring = sbase + C::OFF_RING;
-  const uint32_t s_ds = sbase + C::OFF_DS;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (!smem_aligned_or_report(smem_raw, p.err)) return;
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t s_q = sbase + C::OFF_Q, s_do = sbase + C::OFF_DO;
+  const uint32_t s_kr = sbase + C::OFF_K, s_vr = sbase + C::OFF_V;
   const uint32_t b_qdo = sbase + C::OFF_BAR;
-  const uint32_t b_full = b_qdo + 8, b_empty = b_full + 8 * C::STAGES;
-  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 16;
-  // dS-ready is one barrier per dS buffer: S/dP of blocks j and j+1 are both in
-  // flight, so a warp may finish dS_{j+1} before another warp finishes dS_j;
-  // with a single barrier those arrivals would land in the same phase.
-  const uint32_t b_ds = b_dp + 16, b_fin = b_ds + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
+  const uint32_t b_kfull = b_qdo + 8, b_kempty = b_kfull + 8 * C::KST;
+  const uint32_t b_vfull = b_kempty + 8 * C::KST, b_vempty = b_vfull + 8 * C::VST;
+  const uint32_t b_s = b_vempty + 8 * C::VST, b_dp = b_s + 8, b_sfree = b_dp + 8,
+                 b_dpfree = b_sfree + 8, b_ds = b_dpfree + 8, b_fin = b_ds + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -486,110 +552,133 @@ __global__ void __launch_bounds__(192, 1)
   const int bh = blockIdx.x;
   const int bkv = (bh / p.hq) * (p.hq / p.group) + (bh % p.hq) / p.group;
   const int nblk = (p.n + C::BN - 1) / C::BN;
-  const int nkv = p.causal ? min(nblk, (m0 + C::BM) / C::BN) : nblk;
+  const int nkv = p.causal ? min(nblk, mb + 1) : nblk;   // BM == BN
   const Ctl ctl{abort_flag, p.err};
+  // block j of K lives in K-ring slot j % 3 (phase (j / 3) & 1), of V in j % 2
+  auto kfull = [&](int j) { return b_kfull + 8 * (j % C::KST); };
+  auto kempty = [&](int j) { return b_kempty + 8 * (j % C::KST); };
+  auto kph = [](int j) { return static_cast<uint32_t>((j / C::KST) & 1); };
+  auto vfull = [&](int j) { return b_vfull + 8 * (j % C::VST); };
+  auto vempty = [&](int j) { return b_vempty + 8 * (j % C::VST); };
+  auto vph = [](int j) { return static_cast<uint32_t>((j / C::VST) & 1); };
+  auto k_addr = [&](int j) { return s_kr + (j % C::KST) * C::TILE; };
+  auto v_addr = [&](int j) { return s_vr + (j % C::VST) * C::TILE; };
 
   if (threadIdx.x == 0) {
     mbar_init(b_qdo, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(b_full + 8 * s, 1);
-      mbar_init(b_empty + 8 * s, 1);
+    for (int s = 0; s < C::KST; ++s) {
+      mbar_init(b_kfull + 8 * s, 1);
+      mbar_init(b_kempty + 8 * s, 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(b_s + 8 * t, 1);
-      mbar_init(b_dp + 8 * t, 1);
+    for (int s = 0; s < C::VST; ++s) {
+      mbar_init(b_vfull + 8 * s, 1);
+      mbar_init(b_vempty + 8 * s, 1);
     }
-    mbar_init(b_ds, 128);
-    mbar_init(b_ds + 8, 128);
+    mbar_init(b_s, 1);
+    mbar_init(b_dp, 1);
+    mbar_init(b_sfree, C::NCOMPUTE);
+    mbar_init(b_dpfree, C::NCOMPUTE);
+    mbar_init(b_ds, C::NCOMPUTE);
+    mbar_init(b_ds + 8, C::NCOMPUTE);
     mbar_init(b_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(b_qdo, 2 * C::QBYTES);
+      mbar_arrive_expect_tx(b_qdo, 2 * C::TILE);
 #pragma unroll
       for (int c = 0; c < C::CH; ++c) {
         tma_load_3d(s_q + c * 16384, &tm_q, b_qdo, c * 64, m0, bh);
         tma_load_3d(s_do + c * 16384, &tm_do, b_qdo, c * 64, m0, bh);
       }
-      int it = 0;
       bool ok = true;
+      int loaded_k = 0, loaded_v = 0;
       for (int j = 0; j < nkv && ok; ++j) {
-#pragma unroll 1
-        for (int kind = 0; kind < 2; ++kind, ++it) {  // K_j then V_j
-          const int slot = it % C::STAGES;
-          ok = mbar_wait(b_empty + 8 * slot, ((it / C::STAGES) & 1) ^ 1, ctl, kErrTimeoutLoad);
-          if (!ok) break;
-          const uint32_t fb = b_full + 8 * slot;
-          mbar_arrive_expect_tx(fb, C::KVBYTES);
-          const uint32_t dst = s_ring + slot * C::KVBYTES;
+        ok = mbar_wait(kempty(j), kph(j) ^ 1, ctl, kErrTimeoutLoad);
+        if (!ok) break;
+        mbar_arrive_expect_tx(kfull(j), C::TILE);
 #pragma unroll
-          for (int c = 0; c < C::CH; ++c)
-            tma_load_3d(dst + c * (C::BN * 128), kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
-                        c * 64, j * C::BN, bkv);
-        }
+        for (int c = 0; c < C::CH; ++c)
+          tma_load_3d(k_addr(j) + c * 16384, &tm_k, kfull(j), c * 64, j * C::BN, bkv);
+        ++loaded_k;
+        ok = mbar_wait(vempty(j), vph(j) ^ 1, ctl, kErrTimeoutLoad);
+        if (!ok) break;
+        mbar_arrive_expect_tx(vfull(j), C::TILE);
+#pragma unroll
+        for (int c = 0; c < C::CH; ++c)
+          tma_load_3d(v_addr(j) + c * 16384, &tm_v, vfull(j), c * 64, j * C::BN, bkv);
+        ++loaded_v;
       }
       if (!ok) {
         drain_loads(b_qdo, 1, 1);
-        drain_loads(b_full, it, C::STAGES);
+        drain_loads(b_kfull, loaded_k, C::KST);
+        drain_loads(b_vfull, loaded_v, C::VST);
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nkv > 0) {
-      constexpr uint32_t id_s = idesc_f16(128, C::BN, false, false);
+      constexpr uint32_t id_s = idesc_f16(128, 128, false, false);
       constexpr uint32_t id_q = idesc_f16(128, D, false, true);
-      auto slot_of = [](int it) { return it % C::STAGES; };
-      auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(d_tmem, sdesc_sw128(a_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                 sdesc_sw128(b_s_ + (kk >> 2) * (C::BN * 128) + (kk & 3) * 32, 16, 1024), id_s,
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_s,
                  kk > 0 ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(b_qdo, 0, ctl, kErrTimeoutMma);
-      // S_j and dP_j into TMEM buffer j&1
-      auto issue_sdp = [&](int j) -> bool {
-        const int nb = j & 1;
-        if (!mbar_wait(b_full + 8 * slot_of(2 * j), ph_of(2 * j), ctl, kErrTimeoutMma)) return false;
+      if (ok) ok = mbar_wait(kfull(0), 0, ctl, kErrTimeoutMma);
+      if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_S + 64 * nb, s_q, s_ring + slot_of(2 * j) * C::KVBYTES);
-        mma_commit(b_s + 8 * nb);
-        if (!mbar_wait(b_full + 8 * slot_of(2 * j + 1), ph_of(2 * j + 1), ctl, kErrTimeoutMma))
-          return false;
+        issue_t(tmem + C::COL_S, s_q, k_addr(0));
+        mma_commit(b_s);
+        ok = mbar_wait(vfull(0), 0, ctl, kErrTimeoutMma);
+      }
+      if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_DP + 64 * nb, s_do, s_ring + slot_of(2 * j + 1) * C::KVBYTES);
-        mma_commit(b_dp + 8 * nb);
-        mma_commit(b_empty + 8 * slot_of(2 * j + 1));  // V_j no longer needed
-        return true;
-      };
-      if (ok) ok = issue_sdp(0);
-      if (ok && nkv > 1) ok = issue_sdp(1);
+        issue_t(tmem + C::COL_DP, s_do, v_addr(0));
+        mma_commit(b_dp);
+        mma_commit(vempty(0));  // V_0 no longer needed
+      }
       for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv) {
+          ok = mbar_wait(b_sfree, j & 1, ctl, kErrTimeoutMma) &&
+               mbar_wait(kfull(j + 1), kph(j + 1), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_S, s_q, k_addr(j + 1));
+          mma_commit(b_s);
+          ok = mbar_wait(b_dpfree, j & 1, ctl, kErrTimeoutMma) &&
+               mbar_wait(vfull(j + 1), vph(j + 1), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_DP, s_do, v_addr(j + 1));
+          mma_commit(b_dp);
+          mma_commit(vempty(j + 1));  // V_{j+1} no longer needed
+        }
         ok = mbar_wait(b_ds + 8 * (j & 1), (j >> 1) & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t k_s = s_ring + slot_of(2 * j) * C::KVBYTES;
-        const uint32_t ds_s = s_ds + (j & 1) * C::DSBYTES;
+        const uint32_t ds_t = tmem + C::COL_DS + 64 * (j & 1);
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk)
-          mma_ss(tmem + C::COL_DQ, sdesc_sw128(ds_s + kk * 32, 16, 1024),
-                 sdesc_sw128(k_s + kk * 2048, C::BN * 128, 1024), id_q, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(b_empty + 8 * slot_of(2 * j));  // K_j no longer needed
-        if (j + 2 < nkv) ok = issue_sdp(j + 2);
+          mma_ts(tmem + C::COL_DQ, ds_t + kk * 8, sdesc_sw128(k_addr(j) + kk * 2048, 16384, 1024),
+                 id_q, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(kempty(j));  // K_j no longer needed
       }
       mma_commit(b_fin);
       const uint64_t t0 = globaltimer_ns();
@@ -597,62 +686,71 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ compute (warps 0-3)
-    const int r = threadIdx.x;
+    // ------------------------------------------------------------ compute (warps 0-7)
+    const int w = warp >> 2;
+    const int r = threadIdx.x & 127;
     const int row = m0 + r;
-    const bool row_in = row < p.n;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const float lse2 = row_in ? p.lse[static_cast<size_t>(bh) * p.n + row] * 1.4426950408889634f
-                              : INFINITY;
-    const float dv = row_in ? p.dvec[static_cast<size_t>(bh) * p.n + row] : 0.f;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    // padded rows (row >= N) read LSE = +inf, Dv = 0: their P and dS are 0
+    const size_t prow = static_cast<size_t>(bh) * p.n_pad + row;
+    const float lse2 = p.lse2[prow];
+    const float dvs = p.dvec[prow];   // Dv * scale
+    const int klim = p.causal ? min(p.n - 1, row) : (p.n - 1);  // key live iff key <= klim
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int buf = j & 1;
-      ok = mbar_wait(b_s + 8 * buf, (j >> 1) & 1, ctl, kErrTimeoutSoftmax);
+      const uint32_t ph = j & 1;
+      ok = mbar_wait(b_s, ph, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       uint32_t sr[2][32];
-      tmem_ld32(tmem + C::COL_S + 64 * buf + lane_off, sr[0]);
-      tmem_ld32(tmem + C::COL_S + 64 * buf + 32 + lane_off, sr[1]);
+      tmem_ld32(tmem + C::COL_S + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_S + 64 * w + 32 + lane_off, sr[1]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int k = 0; k < 32; ++k) asm volatile("" : "+r"(sr[c][k]));
-      float pv[64];
-      const int kv0 = j * C::BN;
-      const bool need_mask = (kv0 + C::BN > p.n) || (p.causal && kv0 + C::BN - 1 > m0);
-      const int klim = p.causal ? min(p.n - 1, row) : (p.n - 1);  // valid iff key <= klim
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      tc_fence_before();
+      mbar_arrive(b_sfree);
+      float pv[2][32];
+      const int kv0 = j * C::BN + 64 * w;
+      const bool need_mask = kv0 + 63 > klim;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float e = ex2(fmaf(__uint_as_float(sr[c >> 5][c & 31]), p.scale_log2, -lse2));
-        pv[c] = (!need_mask || kv0 + c <= klim) ? e : 0.f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lse2));
+      if (need_mask) {  // only the diagonal block and the ragged tail
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (kv0 + 32 * h + c > klim) pv[h][c] = 0.f;
       }
-      ok = mbar_wait(b_dp + 8 * buf, (j >> 1) & 1, ctl, kErrTimeoutSoftmax);
+      ok = mbar_wait(b_dp, ph, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      tmem_ld32(tmem + C::COL_DP + 64 * buf + lane_off, sr[0]);
-      tmem_ld32(tmem + C::COL_DP + 64 * buf + 32 + lane_off, sr[1]);
+      tmem_ld32(tmem + C::COL_DP + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_DP + 64 * w + 32 + lane_off, sr[1]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int k = 0; k < 32; ++k) asm volatile("" : "+r"(sr[c][k]));
-#pragma unroll
-      for (int c = 0; c < 64; ++c)
-        pv[c] = pv[c] * (__uint_as_float(sr[c >> 5][c & 31]) - dv) * p.scale;
-      const uint32_t ds_s = s_ds + buf * C::DSBYTES;
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        st_shared_v4(ds_s + r * 128 + ((c8 ^ (r & 7)) << 4), pack_half2(pv[8 * c8], pv[8 * c8 + 1]),
-                     pack_half2(pv[8 * c8 + 2], pv[8 * c8 + 3]),
-                     pack_half2(pv[8 * c8 + 4], pv[8 * c8 + 5]),
-                     pack_half2(pv[8 * c8 + 6], pv[8 * c8 + 7]));
-      fence_async_smem();
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
       tc_fence_before();
-      mbar_arrive(b_ds + 8 * buf);
+      mbar_arrive(b_dpfree);
+      // dS = P * (scale * dP - Dv * scale), packed two fp16 per 32-bit TMEM
+      // column: this group's 64 keys are columns 32w..32w+31 of buffer j&1
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pv[h][c] *= fmaf(__uint_as_float(sr[h][c]), p.scale, -dvs);
+      tmem_st_pairs(tmem + C::COL_DS + 64 * (j & 1) + 32 * w + lane_off, pv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(b_ds + 8 * (j & 1));
     }
     if (ok && nkv > 0) {
       ok = mbar_wait(b_fin, 0, ctl, kErrTimeoutEpilogue);
@@ -661,15 +759,15 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const size_t rowoff = (static_cast<size_t>(bh) * p.n + row) * D;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
+          const int col = w * (D / 2) + 32 * c;
           uint32_t v[32];
-          tmem_ld32(tmem + C::COL_DQ + 32 * c + lane_off, v);
-          tmem_ld_wait(v);
-          if (row_in) {
+          tmem_ld32_sync(tmem + C::COL_DQ + col + lane_off, v);
+          if (row < p.n) {
             if (p.dq_fp32)
-              store_row32_f32(static_cast<float*>(p.dq) + rowoff + 32 * c, v, 1.f);
+              store_row32_f32(static_cast<float*>(p.dq) + rowoff + col, v, 1.f);
             else
-              store_row32_f16(static_cast<__half*>(p.dq) + rowoff + 32 * c, v, 1.f);
+              store_row32_f16(static_cast<__half*>(p.dq) + rowoff + col, v, 1.f);
           }
         }
       }
@@ -679,7 +777,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) {
+  if (warp == 8) {
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

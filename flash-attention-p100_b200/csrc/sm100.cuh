@@ -34,7 +34,17 @@ enum DevErr : int {
   kErrTimeoutMma = 2,    // MMA issuer waited too long for an operand
   kErrTimeoutSoftmax = 3,  // softmax / compute warps waited too long for an MMA
   kErrTimeoutEpilogue = 4,
+  kErrSmemAlign = 5,     // dynamic shared memory did not start 1024-byte aligned
 };
+
+// Kernels that need every byte of shared memory do not pad for alignment:
+// they check that the dynamic window starts on a 1024-byte boundary (the
+// swizzled tile layout requires it) and, if not, report and exit at once.
+__device__ __forceinline__ bool smem_aligned_or_report(const void* smem, int* err) {
+  if ((static_cast<uint32_t>(__cvta_generic_to_shared(smem)) & 1023u) == 0) return true;
+  if (threadIdx.x == 0 && err) atomicCAS(err, 0, static_cast<int>(kErrSmemAlign));
+  return false;
+}
 
 // One wait gives up after this many nanoseconds of global time. Every healthy
 // wait in these kernels is microseconds; a second means the pipeline is stuck.
@@ -151,6 +161,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory
 // ---------------------------------------------------------------------------
@@ -196,6 +216,19 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]. Issued by one thread. A (M=128 x K) sits in
+// lanes 0..127, one row per lane; 32-bit column c of a K=16 step holds
+// elements 2c (low half) and 2c+1 (high half), so a step spans 8 columns.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -265,6 +298,34 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes, to take part of the exponentials off the MUFU unit
+// (one ex2 occupies it for 8 cycles per warp; softmax-heavy loops saturate it).
+// Cody-Waite style reduction x = n + f: adding 1.5*2^23 rounds x to the
+// nearest integer n inside the low mantissa bits of t, f = x - n is in
+// [-0.5, 0.5], 2^f comes from a degree-4 polynomial fitted for this library by
+// iteratively reweighted least squares on [-0.5, 0.5] (max relative error
+// 2.7e-6, below fp16's 4.9e-4 half-ulp), and 2^n is added into the exponent
+// field with one integer multiply-add (the low 9 bits of t hold n mod 512).
+// x is clamped to >= -125 so the exponent never underflows; results below
+// 2^-125 are far under fp16's range and every caller masks with 0 explicitly.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(f, 0.009570376f, 0.055918723f);
+  p = fmaf(p, f, 0.24024746f);
+  p = fmaf(p, f, 0.69312167f);
+  p = fmaf(p, f, 0.99999928f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Mixed exponential for fully unrolled column loops (c is then a constant and
+// the choice folds away): columns with c % 3 == 0 use the polynomial, the
+// rest the MUFU ex2, which roughly balances the two pipes.
+__device__ __forceinline__ float exp2_mixed(float x, int c) {
+  return (c % 3 == 0) ? exp2_poly(x) : ex2(x);
 }
 
 // Byte offset of 16-byte piece `c` (0..D/8-1) of row `r` in a swizzled tile of

@@ -37,7 +37,7 @@ enum {
   FA_B200_ERR_WORKSPACE = 7,       /* workspace missing or smaller than required */
   FA_B200_ERR_DEVICE = 8,          /* current device is not compute capability 10.x */
   FA_B200_ERR_TOO_LARGE = 9,       /* a grid dimension would exceed CUDA limits */
-  FA_B200_ERR_SCRATCH_LIMIT = 10   /* B*Hq*N above fa_b200_backward_noalloc_max_rows() */
+  FA_B200_ERR_SCRATCH_LIMIT = 10   /* B*Hq*roundup(N,128) above fa_b200_backward_noalloc_max_rows() */
 };
 
 /* Forward. Replaces fa_forward (reference fa_p100_ext.cu:53-83) and
@@ -49,8 +49,10 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
                     int B, int Hq, int Hkv, int N, int D, int causal, int full_precision,
                     void* stream);
 
-/* Bytes of device workspace fa_b200_backward needs: B*Hq*N fp32 for the
- * row sums Dv = rowsum(dO o O) (reference fa_p100_ext.cu:124). */
+/* Bytes of device workspace fa_b200_backward needs: per query row the row sum
+ * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the
+ * log2-scaled LSE, each head padded to roundup(N, 128) rows:
+ * 2 * 4 * B * Hq * roundup(N, 128) bytes. */
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
 
 /* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
@@ -86,22 +88,22 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
  * (a framework's caching pool, an engine that only passes its plugins the
  * tensors of the op) or a serving loop that must not call cudaMalloc, whose
  * implicit synchronisation would stall every stream on the device.
- * Same inputs, outputs and results as fa_b200_backward; the Dv row sums go to
- * a 16 MiB array compiled into the library (resident on every GPU that loads
- * it until the process exits), so B*Hq*N may be at most
- * fa_b200_backward_noalloc_max_rows() = 4,194,304 (FA_B200_ERR_SCRATCH_LIMIT
+ * Same inputs, outputs and results as fa_b200_backward; the per-row workspace
+ * goes to a 16 MiB array compiled into the library (resident on every GPU that
+ * loads it until the process exits), so B*Hq*roundup(N,128) may be at most
+ * fa_b200_backward_noalloc_max_rows() = 2,097,152 (FA_B200_ERR_SCRATCH_LIMIT
  * otherwise). The first call on a device looks up that array's device address
  * (and does the library's one-time device set-up); make that first call before
  * any stream capture. Every call on a device shares the one array: calls whose
  * backward passes overlap on the GPU (different streams, or different host
  * threads) race on it and must be serialised by the caller. Nothing in it has
- * to start at zero: each call writes every row sum it reads. */
+ * to start at zero: each call writes every workspace entry it reads. */
 int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const void* dO,
                              const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                              void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
                              void* stream);
 
-/* Largest B*Hq*N fa_b200_backward_noalloc accepts. */
+/* Largest B*Hq*roundup(N,128) fa_b200_backward_noalloc accepts. */
 size_t fa_b200_backward_noalloc_max_rows(void);
 
 /* Reads the device error word the kernels set when a bounded internal wait
@@ -122,8 +124,9 @@ const char* fa_b200_last_error(void);
  * A * B^T for one 128x128x128 fp16 tile through the same TMA swizzle, shared-
  * memory descriptors and tcgen05 MMA the attention kernels use. a_mn / b_mn
  * select MN-major operands (a given as [K][M], b as [K][N]); otherwise a is
- * [M][K] and b is [N][K]. a_by_threads != 0 stages A with thread stores (the
- * path P and dS take) instead of TMA. */
+ * [M][K] and b is [N][K]. a_by_threads = 1 stages A in shared memory with
+ * thread stores (the path P and dS take) instead of TMA; 2 stores A into
+ * tensor memory with tcgen05.st and issues the A-from-TMEM form of the MMA. */
 int fa_b200_selftest_gemm(const void* a, const void* b, float* c, int a_mn, int b_mn,
                           int a_by_threads, void* stream);
 

@@ -59,22 +59,24 @@ def test_backward_argument_errors():
     assert bwd(D=80) == 2
     assert bwd(Hq=3, Hkv=2) == 3
     assert bwd(ws=None) == 7
-    assert bwd(ws_bytes=4 * 4 * 16 - 4) == 7       # one float short of B*Hq*N
+    need = _lib.lib().fa_b200_backward_workspace_bytes(1, 4, 16)
+    assert bwd(ws_bytes=need - 4) == 7             # one float short
     assert bwd(ws=MISALIGNED) == 4
     assert bwd(stages=8) == 3                       # unknown stage bit
 
 
 def test_workspace_size():
     lib = _lib.lib()
-    assert lib.fa_b200_backward_workspace_bytes(2, 8, 100) == 6400   # 2*8*100*4, 256-aligned
-    assert lib.fa_b200_backward_workspace_bytes(1, 1, 1) == 256
+    # Dv and LSE*log2e per row, each head padded to a multiple of 128 rows
+    assert lib.fa_b200_backward_workspace_bytes(2, 8, 100) == 2 * 4 * 2 * 8 * 128
+    assert lib.fa_b200_backward_workspace_bytes(1, 1, 129) == 2 * 4 * 256
     assert lib.fa_b200_backward_workspace_bytes(0, 1, 1) == 0
 
 
 def test_noalloc_limit_and_errors():
     lib = _lib.lib()
     rows = lib.fa_b200_backward_noalloc_max_rows()
-    assert rows == 1 << 22
+    assert rows == 1 << 21
     st = lib.fa_b200_backward_noalloc(P, P, P, P, P, P, P, 1, P, P, 1, 32, 32, rows // 32 + 1,
                                       64, 1, None)
     assert st == 10

@@ -10,7 +10,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("a_mn,b_mn,a_threads", [(0, 0, 0), (0, 1, 0), (1, 1, 0), (1, 0, 0),
-                                                 (0, 0, 1), (0, 1, 1)])
+                                                 (0, 0, 1), (0, 1, 1), (0, 0, 2), (0, 1, 2)])
 def test_selftest_gemm(cuda, a_mn, b_mn, a_threads):
     g = torch.Generator(device="cpu").manual_seed(1234 + 8 * a_mn + 4 * b_mn + a_threads)
     A = torch.randn(128, 128, generator=g).half()   # math A[m][k]
