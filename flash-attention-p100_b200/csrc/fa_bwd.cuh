@@ -264,10 +264,21 @@ __global__ void __launch_bounds__(320, 1)
       }
       int it = 0;
       bool ok = true;
+      constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
+      auto prefetch_step = [&](int st) {
+        const int q0p = (i_start + st % nq_head) * C::BM;
+        const int bhp = b * p.hq + kvh * p.group + st / nq_head;
+        for (int c = 0; c < C::CH; ++c) {
+          tma_prefetch_l2_3d(&tm_q, c * 64, q0p, bhp);
+          tma_prefetch_l2_3d(&tm_do, c * 64, q0p, bhp);
+        }
+      };
+      for (int st = 0; st < kAhead && st < total; ++st) prefetch_step(st);
       for (int step = 0; step < total && ok; ++step) {
         const int g = step / nq_head;
         const int q0 = (i_start + step % nq_head) * C::BM;
         const int bh = b * p.hq + kvh * p.group + g;
+        if (step + kAhead < total) prefetch_step(step + kAhead);
 #pragma unroll 1
         for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
           const int slot = slot_of(it);
@@ -605,7 +616,18 @@ __global__ void __launch_bounds__(320, 1)
       }
       bool ok = true;
       int loaded_k = 0, loaded_v = 0;
+      constexpr int kAhead = 3;  // L2 prefetch distance, in key blocks
+      for (int j = 0; j < kAhead && j < nkv; ++j)
+        for (int c = 0; c < C::CH; ++c) {
+          tma_prefetch_l2_3d(&tm_k, c * 64, j * C::BN, bkv);
+          tma_prefetch_l2_3d(&tm_v, c * 64, j * C::BN, bkv);
+        }
       for (int j = 0; j < nkv && ok; ++j) {
+        if (j + kAhead < nkv)
+          for (int c = 0; c < C::CH; ++c) {
+            tma_prefetch_l2_3d(&tm_k, c * 64, (j + kAhead) * C::BN, bkv);
+            tma_prefetch_l2_3d(&tm_v, c * 64, (j + kAhead) * C::BN, bkv);
+          }
         ok = mbar_wait(kempty(j), kph(j) ^ 1, ctl, kErrTimeoutLoad);
         if (!ok) break;
         mbar_arrive_expect_tx(kfull(j), C::TILE);

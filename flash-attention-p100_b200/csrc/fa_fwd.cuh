@@ -162,7 +162,18 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_3d((t ? s_q1 : s_q0) + c * 16384, &tm_q, b_q, c * 64, m0 + 128 * t, bh);
       int it = 0;
       bool ok = true;
+      constexpr int kAhead = 2;  // L2 prefetch distance, in key blocks
+      for (int j = 0; j < kAhead && j < nkv; ++j)
+        for (int c = 0; c < C::CH; ++c) {
+          tma_prefetch_l2_3d(&tm_k, c * 64, j * 128, kvh);
+          tma_prefetch_l2_3d(&tm_v, c * 64, j * 128, kvh);
+        }
       for (int j = 0; j < nkv && ok; ++j) {
+        if (j + kAhead < nkv)
+          for (int c = 0; c < C::CH; ++c) {
+            tma_prefetch_l2_3d(&tm_k, c * 64, (j + kAhead) * 128, kvh);
+            tma_prefetch_l2_3d(&tm_v, c * 64, (j + kAhead) * 128, kvh);
+          }
 #pragma unroll 1
         for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
           const int slot = it % C::STAGES;

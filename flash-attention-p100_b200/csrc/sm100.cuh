@@ -161,6 +161,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Pull a 3-D tile into L2 ahead of its real load (no shared memory, no barrier):
+// producers whose ring is too shallow to cover a DRAM round trip prefetch a
+// few steps ahead so the load into shared memory later hits L2.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 // 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
