@@ -52,6 +52,7 @@ WORKLOADS = {
     "C3a": (4, 32, 8, 3000, 128, False, 0.5),
     "C3b": (2, 16, 1, 1537, 64, False, 0.5),
     "north_star": (1, 32, 32, 8192, 128, True, 1.0),
+    "C5": (1, 32, 8, 131072, 128, True, 1.0),
 }
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
@@ -247,6 +248,53 @@ def kernel_work(name, B, Hq, Hkv, N, D, causal):
     return 2.0 * B * Hq * N * D * 2 + B * Hq * N * 4, "GB/s", "hbm"
 
 
+def qwen3_step_ms(dev, attn, steps, warmup, seq=8192):
+    """a Qwen3-0.6B-shaped decoder (28 layers, hidden 1024,
+    16 query / 8 kv heads of 128, q/k RMSNorm, RoPE theta 1e6, SwiGLU 3072,
+    vocab 151936 tied), random init N(0, 0.02), token ids uniform in the vocab,
+    B=1, `seq` tokens, one fp16-autocast forward + backward with the model's
+    own next-token cross-entropy. attn = "fa_p100" (the HF registration) or
+    "sdpa". Returns the median step time in ms (CUDA events)."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    import fa_p100_hf
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, max_position_embeddings=40960, initializer_range=0.02,
+                      rope_parameters={"rope_theta": 1e6, "rope_type": "default"},
+                      tie_word_embeddings=True, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Qwen3ForCausalLM(cfg)
+    if attn == "fa_p100":
+        fa_p100_hf.enable_fa_p100(model)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (1, seq), device=dev, generator=gen)
+
+    def step():
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.float16):
+            loss = model(input_ids=ids, labels=ids).loss
+        loss.backward()
+        return loss
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        loss = step()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    if not torch.isfinite(loss).item():
+        raise RuntimeError(f"qwen3 step ({attn}) produced a non-finite loss")
+    del model
+    torch.cuda.empty_cache()
+    return statistics.median(times), float(loss.item())
+
+
 def run_ours(args, world, rank, local):
     import _lib
     import fa_p100
@@ -401,10 +449,85 @@ def run_ours(args, world, rank, local):
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_qwen3:
+        q_ms, q_loss = qwen3_step_ms(dev, "fa_p100", 5, 3)
+        s_ms, s_loss = qwen3_step_ms(dev, "sdpa", 5, 3)
+        line["qwen3_0p6b_step_ms"] = {
+            "value": q_ms, "sdpa_ms": s_ms, "loss": q_loss, "sdpa_loss": s_loss,
+            "config": "BASELINE config 4: 28 layers, hidden 1024, 16/8 heads x 128, seq 8192, "
+                      "B=1, fp16 autocast fwd+bwd, random init, attention via fa_p100 registration"}
     if world == 1 and not args.no_cpu_baseline:
         cpu_tf, _, cores, sample = cpu_step_tflops(args.workload, 3, 1, min_seconds=10.0)
         line["cpu_baseline"] = {"value": cpu_tf, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": sample}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ring(args, world, rank, local):
+    """Config 5: one causal sequence zigzag-sharded over the ranks, ring
+    context parallelism (fa_b200_ring). value = the whole problem's algorithmic
+    FLOPs / the max-over-ranks step time (strong scaling). At one GPU the same
+    problem runs through the single-GPU kernels, the efficiency reference."""
+    import _lib
+    import fa_b200_ring as ring
+    import fa_p100
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[args.workload]
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    n_loc = N // world
+
+    def rnd(h):
+        return (torch.randn(B, h, n_loc, D, device=dev, generator=gen) * sc).half()
+
+    q, k, v, do = rnd(Hq).requires_grad_(True), rnd(Hkv).requires_grad_(True), \
+        rnd(Hkv).requires_grad_(True), rnd(Hq)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        o = ring.ring_flash_attn(q, k, v) if world > 1 else fa_p100.flash_attn(q, k, v, True)
+        o.backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    times = []
+    with ClockSampler([local]) as clocks:
+        barrier(world)
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        barrier(world)
+    if _lib.device_error(local) != 0:
+        raise RuntimeError("device error word set during the ring steps")
+    ms = max_over_ranks(sum(times) / len(times), world, dev)
+    total = ring.ring_flops(B, Hq, N, D)
+    pieces_fwd = 1 + 2 * (world - 1)
+    if rank != 0:
+        return 0
+    peak_tf, _, peak_src = load_peak()
+    value = total / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
+        "pct_of_peak": 100.0 * value / world / peak_tf, "peak_tflops": peak_tf,
+        "peak_source": peak_src,
+        "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
+                   "causal": causal, "parallelism": f"ring context parallel, zigzag x{world}"
+                   if world > 1 else "single GPU",
+                   "l2": "flushed (256 MiB write) before each step"},
+        "gpu_launches": args.steps * (pieces_fwd + 3 * pieces_fwd) if world > 1 else 4 * args.steps,
+        "clocks": clocks.summary(),
+    }
     print(json.dumps(line), flush=True)
     return 0
 
@@ -417,6 +540,10 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="C2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ring", action="store_true",
+                    help="ring context parallelism over the ranks (use with --workload C5)")
+    ap.add_argument("--no-qwen3", action="store_true",
+                    help="skip the Qwen3-0.6B-shaped training step (BASELINE config 4)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -425,6 +552,8 @@ def main():
     try:
         if args.impl == "reference":
             return run_reference(args, world, rank)
+        if args.ring:
+            return run_ring(args, world, rank, local)
         return run_ours(args, world, rank, local)
     finally:
         if world > 1 and args.impl == "ours":

@@ -150,3 +150,29 @@ def reference_step(q, k, v, do, causal=False):
     o = torch.softmax(s, dim=-1) @ ve
     o.backward(do.detach().to("cpu", torch.float32))
     return o.detach(), qf.grad, kf.grad, vf.grad
+
+
+def attention_grads_given_lse(q, k, v, do, o, lse, causal=False):
+    """Backward of one attention piece given the softmax statistics of the
+    whole row (what a ring step sees): P = exp(scale S - LSE), Dv = rowsum(dO o O),
+    dS = P o (dO V^T - Dv), dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO --
+    the reference backward's formulas (flash_bwd.cuh:66-78, :267-281) with the
+    forward's LSE passed in rather than recomputed. fp32, CPU, GQA-aware."""
+    q, k, v, do, o = (t.detach().to("cpu", torch.float32) for t in (q, k, v, do, o))
+    lse = lse.detach().to("cpu", torch.float32)
+    B, Hq, N, D = q.shape
+    g = _group(q, k)
+    scale = 1.0 / math.sqrt(D)
+    dq = torch.zeros_like(q)
+    dk = torch.zeros_like(k)
+    dv = torch.zeros_like(v)
+    for b in range(B):
+        for h in range(Hq):
+            kh, vh = k[b, h // g], v[b, h // g]
+            p = torch.exp(_scores(q[b, h], kh, causal) - lse[b, h][:, None])
+            dvec = (do[b, h] * o[b, h]).sum(-1, keepdim=True)
+            ds = p * (do[b, h] @ vh.transpose(0, 1) - dvec)
+            dq[b, h] = scale * (ds @ kh)
+            dk[b, h // g] += scale * (ds.transpose(0, 1) @ q[b, h])
+            dv[b, h // g] += p.transpose(0, 1) @ do[b, h]
+    return dq, dk, dv
