@@ -229,7 +229,7 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 # GPU side: our kernels
 # ---------------------------------------------------------------------------
-STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ = 1, 2, 4
+STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ, STAGE_FUSED = 1, 2, 4, 8
 KERNELS = ("fwd", "bwd_rowsum", "bwd_dkdv", "bwd_dq")
 
 

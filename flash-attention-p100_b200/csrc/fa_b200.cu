@@ -108,6 +108,8 @@ int device_setup(int* dev_out, int** err_out) {
         set_smem(bwd_dkdv_kernel<128>, DkdvCfg<128>::SMEM);
         set_smem(bwd_dq_kernel<64>, DqCfg<64>::SMEM);
         set_smem(bwd_dq_kernel<128>, DqCfg<128>::SMEM);
+        set_smem(bwd_fused_kernel<64>, FusedCfg<64>::SMEM);
+        set_smem(bwd_fused_kernel<128>, FusedCfg<128>::SMEM);
         st.status = (cudaGetLastError() == cudaSuccess) ? FA_B200_OK : FA_B200_ERR_DEVICE;
       }
     }
@@ -140,6 +142,16 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Both dq dtypes take the separate dK/dV and dQ kernels: no atomics, bitwise
+// deterministic, and on B200 faster than the fused kernel, whose per-step
+// fp32 atomic adds of dQ (4.4 GB at B=1, H=32, N=8192) cost more than the
+// dQ kernel's recompute (measured: fused 2.32 ms, of which 0.85 ms is the
+// atomics, against 1.95 ms for dK/dV + dQ).
+int default_stages(int dq_fp32) {
+  (void)dq_fp32;
+  return FA_B200_STAGE_ALL;
+}
 
 // Device address of g_noalloc_scratch on `dev`, looked up once per device with
 // that device current (device_setup has just made it current on this thread).
@@ -228,12 +240,18 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const long long threads = rows_pad * (D / 8);
     bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const __half*>(o), static_cast<const __half*>(dO), lse, p.dvec, p.lse2, N,
-        n_pad, rows_pad, p.scale);
+        n_pad, rows_pad, p.scale,
+        p.dq_fp32 ? static_cast<float*>(dq) : nullptr);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_DKDV) {
     bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
                          DkdvCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
+    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+  }
+  if (stages & FA_B200_STAGE_FUSED) {
+    bwd_fused_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), FusedCfg<D>::THREADS,
+                          FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_DQ) {
@@ -387,15 +405,17 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream) {
   return fa_b200_backward_stages(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace,
-                                 workspace_bytes, B, Hq, Hkv, N, D, causal, FA_B200_STAGE_ALL,
-                                 stream);
+                                 workspace_bytes, B, Hq, Hkv, N, D, causal,
+                                 fab::default_stages(dq_fp32), stream);
 }
 
 int fa_b200_backward_stages(const void* q, const void* k, const void* v, const void* dO,
                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
                             int Hkv, int N, int D, int causal, int stages, void* stream) {
-  if (stages & ~FA_B200_STAGE_ALL) return FA_B200_ERR_SHAPE;
+  if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
+  if ((stages & FA_B200_STAGE_FUSED) && (!dq_fp32 || (stages & (FA_B200_STAGE_DKDV | FA_B200_STAGE_DQ))))
+    return FA_B200_ERR_SHAPE;
   if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
   int st = fab::check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
@@ -444,10 +464,11 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
   float* ws = fab::noalloc_scratch(dev);
   if (!ws) return FA_B200_ERR_DEVICE;
   auto s = static_cast<cudaStream_t>(stream);
+  const int stages = fab::default_stages(dq_fp32);
   return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                            Hkv, N, causal, FA_B200_STAGE_ALL, s, err)
+                                            Hkv, N, causal, stages, s, err)
                  : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                             Hkv, N, causal, FA_B200_STAGE_ALL, s, err);
+                                             Hkv, N, causal, stages, s, err);
 }
 
 int fa_b200_device_error(int device, int reset) {

@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
                                                               float* __restrict__ dvec,
                                                               float* __restrict__ lse2, int n,
                                                               int n_pad, long long rows_pad,
-                                                              float scale) {
+                                                              float scale,
+                                                              float* __restrict__ dq_zero) {
   constexpr int TPR = D / 8;  // threads per row (8 or 16)
   const long long gtid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long prow = gtid / TPR;
@@ -72,6 +73,11 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
   const long long row = bh * n + r;
   float acc = 0.f;
   if (real) {
+    if (dq_zero) {  // the fused kernel accumulates dQ into a zeroed fp32 buffer
+      float4* z = reinterpret_cast<float4*>(dq_zero + row * D) + 2 * part;
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + row * D) + part);
     const uint4 b = __ldg(reinterpret_cast<const uint4*>(dO + row * D) + part);
     const __half2* ha = reinterpret_cast<const __half2*>(&a);
@@ -791,6 +797,382 @@ __global__ void __launch_bounds__(320, 1)
             else
               store_row32_f16(static_cast<__half*>(p.dq) + rowoff + col, v, 1.f);
           }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 8) {
+    __syncwarp();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fab
+
+namespace fab {
+
+// ---------------------------------------------------------------------------
+// Fused dK / dV / dQ: the dK/dV kernel's CTA (128 keys, looping over the GQA
+// group and the query blocks), which also forms each step's dQ contribution
+// dQ_i = scale dS_i K and adds it into a zeroed fp32 dQ with vector atomic
+// adds -- the reference's scheme (flash_bwd.cuh:378-444), without recomputing
+// S and dP in a second kernel. Used when the caller takes dQ in fp32.
+//   warps 0-7  compute: two warpgroups; thread r is key row r for P and dS and
+//              query row r when it reads dQ_i out
+//   warp  8    TMEM allocation + MMA issue
+//   warp  9    TMA producer (as in bwd_dkdv_kernel)
+// TMEM: S^T 0..127 (P^T fp16 pairs over cols 32..95) | dP^T 128..255, then
+//       dQ_i once dS_i is formed | dV 256.. | dK 256+D..
+// Shared: K, V, 4-slot Q/dO ring, LSE/Dv slices [2], one dS^T tile [key][query].
+// MMA order per step i:
+//   [P_i] dV += P^T dO (A = P^T in TMEM) ; [dS_i] dK += dS^T Q (A = dS^T tile,
+//   K-major) ; dQ_i = dS K into the dP^T columns (A = the same tile read
+//   MN-major, B = K MN-major) ; [Q_{i+1}] S^T_{i+1} ; [dQ_i read] dP^T_{i+1}
+// Overwrites follow issue order (S^T_{i+1} after dV_i read P_i; dQ_i after
+// the compute threads read dP_i; dP^T_{i+1} after they read dQ_i out). The dS
+// tile is rewritten at step i+1 only after this thread saw dQ_i complete.
+// ---------------------------------------------------------------------------
+#ifndef FAB_DQ_RED
+#define FAB_DQ_RED red_add_v4
+#endif
+
+template <int D>
+struct FusedCfg {
+  static constexpr int BN = 128, BM = 128, CH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int STAGES = 4;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE;
+  static constexpr int OFF_RING = OFF_V + TILE;
+  static constexpr int OFF_DS = OFF_RING + STAGES * TILE;    // 128 keys x 128 queries fp16
+  static constexpr int OFF_LSE = OFF_DS + 32768;             // [2][128] LSE*log2e, [2][128] Dv*scale
+  static constexpr int OFF_BAR = OFF_LSE + 2048;
+  // kv, full[ST], empty[ST], s, dp, p, ds, dqfull, dqfree, fin
+  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
+  static constexpr int THREADS = 320;
+  static constexpr int NCOMPUTE = 256;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
+  static constexpr uint32_t COL_P = 32, COL_DQ = 128;
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const BwdParams p) {
+  using C = FusedCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (!smem_aligned_or_report(smem_raw, p.err)) return;
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t s_k = sbase + C::OFF_K, s_v = sbase + C::OFF_V, s_ring = sbase + C::OFF_RING;
+  const uint32_t s_ds = sbase + C::OFF_DS, s_lse = sbase + C::OFF_LSE;
+  const uint32_t b_kv = sbase + C::OFF_BAR;
+  const uint32_t b_full = b_kv + 8, b_empty = b_full + 8 * C::STAGES;
+  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 8, b_p = b_dp + 8, b_ds = b_p + 8,
+                 b_dqfull = b_ds + 8, b_dqfree = b_dqfull + 8, b_fin = b_dqfree + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bkv = blockIdx.x;
+  const int kvb = blockIdx.y;
+  const int hkv = p.hq / p.group;
+  const int b = bkv / hkv, kvh = bkv % hkv;
+  const int kv0 = kvb * C::BN;
+  const int nqb = (p.n + C::BM - 1) / C::BM;
+  const int i_start = p.causal ? kvb : 0;
+  const int nq_head = nqb - i_start;
+  const int total = p.group * nq_head;
+  const Ctl ctl{abort_flag, p.err};
+  auto slot_of = [](int it) { return it % C::STAGES; };
+  auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(b_kv, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(b_full + 8 * s, 1);
+      mbar_init(b_empty + 8 * s, 1);
+    }
+    mbar_init(b_s, 1);
+    mbar_init(b_dp, 1);
+    mbar_init(b_p, C::NCOMPUTE);
+    mbar_init(b_ds, C::NCOMPUTE);
+    mbar_init(b_dqfull, 1);
+    mbar_init(b_dqfree, C::NCOMPUTE);
+    mbar_init(b_fin, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(b_kv, 2 * C::TILE);
+#pragma unroll
+      for (int c = 0; c < C::CH; ++c) {
+        tma_load_3d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, bkv);
+        tma_load_3d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, bkv);
+      }
+      int it = 0;
+      bool ok = true;
+      constexpr int kAhead = 2;
+      auto prefetch_step = [&](int st) {
+        const int q0p = (i_start + st % nq_head) * C::BM;
+        const int bhp = b * p.hq + kvh * p.group + st / nq_head;
+        for (int c = 0; c < C::CH; ++c) {
+          tma_prefetch_l2_3d(&tm_q, c * 64, q0p, bhp);
+          tma_prefetch_l2_3d(&tm_do, c * 64, q0p, bhp);
+        }
+      };
+      for (int st = 0; st < kAhead && st < total; ++st) prefetch_step(st);
+      for (int step = 0; step < total && ok; ++step) {
+        const int g = step / nq_head;
+        const int q0 = (i_start + step % nq_head) * C::BM;
+        const int bh = b * p.hq + kvh * p.group + g;
+        if (step + kAhead < total) prefetch_step(step + kAhead);
+#pragma unroll 1
+        for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
+          const int slot = slot_of(it);
+          ok = mbar_wait(b_empty + 8 * slot, ph_of(it) ^ 1, ctl, kErrTimeoutLoad);
+          if (!ok) break;
+          const uint32_t fb = b_full + 8 * slot;
+          const uint32_t dst = s_ring + slot * C::TILE;
+          mbar_arrive_expect_tx(fb, kind ? C::TILE : C::TILE + 1024);
+#pragma unroll
+          for (int c = 0; c < C::CH; ++c)
+            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
+                        c * 64, q0, bh);
+          if (!kind) {
+            const size_t off = static_cast<size_t>(bh) * p.n_pad + q0;
+            const uint32_t ls = s_lse + (step & 1) * 512;
+            bulk_load(ls, p.lse2 + off, 512, fb);
+            bulk_load(ls + 1024, p.dvec + off, 512, fb);
+          }
+        }
+      }
+      if (!ok) {
+        drain_loads(b_kv, 1, 1);
+        drain_loads(b_full, it, C::STAGES);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && total > 0) {
+      constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (TS), dK (SS)
+      constexpr uint32_t id_q = idesc_f16(128, D, true, true);      // dQ: A = dS MN-major
+      auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_t,
+                 kk > 0 ? 1u : 0u);
+        }
+      };
+      auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
+      bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
+      if (ok) ok = mbar_wait(b_full + 8 * slot_of(0), ph_of(0), ctl, kErrTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_t(tmem + C::COL_S, s_k, slot_addr(0));
+        mma_commit(b_s);
+        ok = mbar_wait(b_full + 8 * slot_of(1), ph_of(1), ctl, kErrTimeoutMma);
+      }
+      if (ok) {
+        tc_fence_after();
+        issue_t(tmem + C::COL_DP, s_v, slot_addr(1));
+        mma_commit(b_dp);
+      }
+      for (int i = 0; i < total && ok; ++i) {
+        const int it_q = 2 * i, it_do = 2 * i + 1;
+        const bool more = i + 1 < total;
+        // dV_i += P_i^T dO_i
+        ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C::BM / 16; ++kk)
+          mma_ts(tmem + C::COL_DV, tmem + C::COL_P + kk * 8,
+                 sdesc_sw128(slot_addr(it_do) + kk * 2048, 16384, 1024), id_g,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(b_empty + 8 * slot_of(it_do));
+        // dK_i += dS_i^T Q_i ; dQ_i = dS_i K
+        ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C::BM / 16; ++kk)
+          mma_ss(tmem + C::COL_DK, sdesc_sw128(s_ds + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                 sdesc_sw128(slot_addr(it_q) + kk * 2048, 16384, 1024), id_g,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(b_empty + 8 * slot_of(it_q));
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          mma_ss(tmem + C::COL_DQ, sdesc_sw128(s_ds + kk * 2048, 16384, 1024),
+                 sdesc_sw128(s_k + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
+        mma_commit(b_dqfull);
+        if (more) {
+          ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_S, s_k, slot_addr(it_q + 2));
+          mma_commit(b_s);
+          ok = mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma) &&
+               mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_t(tmem + C::COL_DP, s_v, slot_addr(it_do + 2));
+          mma_commit(b_dp);
+        }
+      }
+      mma_commit(b_fin);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(b_fin, 0) && globaltimer_ns() - t0 < FAB_WAIT_LIMIT_NS) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ compute (warps 0-7)
+    const int w = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const int kvrow = kv0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int qlim = p.causal ? kvrow : -1;
+    float* dq = static_cast<float*>(p.dq);
+    bool ok = true;
+    for (int i = 0; i < total; ++i) {
+      const int qb0 = (i_start + i % nq_head) * C::BM;   // query block start
+      const int q0 = qb0 + 64 * w;                         // this group's 64 queries
+      const int bh = b * p.hq + kvh * p.group + i / nq_head;
+      const int it_q = 2 * i;
+      const uint32_t ph = i & 1;
+      const bool need_mask = (q0 + 64 > p.n) || (p.causal && q0 < kv0 + 127);
+      // ---- P phase
+      ok = mbar_wait(b_full + 8 * slot_of(it_q), ph_of(it_q), ctl, kErrTimeoutSoftmax) &&
+           mbar_wait(b_s, ph, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(tmem + C::COL_S + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_S + 64 * w + 32 + lane_off, sr[1]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      const float4* lse4 =
+          reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4;
+      const float4* dvs4 = lse4 + 64;
+      float pv[2][32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l4 = lse4[8 * h + c4];
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4)
+            pv[h][4 * c4 + e4] = ex2(fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale_log2, -lv[e4]));
+        }
+      if (need_mask) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int q = q0 + 32 * h + c;
+            if (q < qlim || q >= p.n) pv[h][c] = 0.f;
+          }
+      }
+      tmem_st_pairs(tmem + C::COL_P + 32 * w + lane_off, pv);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(b_p);
+      // ---- dS phase
+      ok = mbar_wait(b_dp, ph, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      tmem_ld32(tmem + C::COL_DP + 64 * w + lane_off, sr[0]);
+      tmem_ld32(tmem + C::COL_DP + 64 * w + 32 + lane_off, sr[1]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 d4 = dvs4[8 * h + c4];
+          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e4 = 0; e4 < 4; ++e4)
+            pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, -dv[e4]);
+        }
+      // dS^T row r (this group's 64 queries) into the swizzled [key][query] tile
+      const uint32_t my_tile = s_ds + w * 16384;
+      st_row32_sw128(my_tile, r, 0, pv[0]);
+      st_row32_sw128(my_tile, r, 1, pv[1]);
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(b_ds);
+      // ---- dQ read-out: lane r of dQ_i is query qb0 + r; this group takes
+      // dQ columns w*D/2 .. (w+1)*D/2 - 1 and adds them into the fp32 dQ
+      ok = mbar_wait(b_dqfull, ph, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      constexpr int NCH = D / 64;   // 32-column chunks per group
+#pragma unroll
+      for (int h = 0; h < NCH; ++h) tmem_ld32(tmem + C::COL_DQ + w * (D / 2) + 32 * h + lane_off, sr[h]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int h = 0; h < NCH; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      tc_fence_before();
+      mbar_arrive(b_dqfree);
+      const int qrow = qb0 + r;
+      if (qrow < p.n) {
+        float* dst = dq + (static_cast<size_t>(bh) * p.n + qrow) * D + w * (D / 2);
+#pragma unroll
+        for (int h = 0; h < NCH; ++h)
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            FAB_DQ_RED(dst + 32 * h + 4 * c4, __uint_as_float(sr[h][4 * c4]),
+                       __uint_as_float(sr[h][4 * c4 + 1]), __uint_as_float(sr[h][4 * c4 + 2]),
+                       __uint_as_float(sr[h][4 * c4 + 3]));
+      }
+    }
+    if (ok && total > 0) {
+      ok = mbar_wait(b_fin, 0, ctl, kErrTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const size_t rowoff = (static_cast<size_t>(bkv) * p.n + kvrow) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          const int col = w * (D / 2) + 32 * c;
+          uint32_t v[32];
+          tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
+          if (kvrow < p.n) store_row32_f16(p.dv + rowoff + col, v, 1.f);
+          tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
+          if (kvrow < p.n) store_row32_f16(p.dk + rowoff + col, v, 1.f);
         }
       }
     }

@@ -10,7 +10,8 @@ SIMT kernels replaced by tcgen05 tensor-core kernels in libfa_b200.so.
 D is 64 or 128, N is arbitrary, Hq a multiple of Hkv (MHA, GQA, MQA).
 `full_precision` is accepted and ignored: the tensor cores multiply fp16
 exactly and accumulate in fp32, which is the reference's fp32-MAC tier.
-The backward is deterministic (no atomics).
+The backward is deterministic: dQ comes from its own kernel rather than
+from the reference's fp32 atomics.
 """
 import math
 

@@ -57,8 +57,10 @@ size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
 
 /* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
  * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq (fp32 when dq_fp32 != 0,
- * as the reference returns it, else fp16), dk and dv (fp16). dq is computed
- * without atomics and is bitwise deterministic. */
+ * as the reference returns it, else fp16), dk and dv (fp16). dQ comes from its
+ * own kernel that owns each dQ row (the reference adds it with fp32 atomics,
+ * flash_bwd.cuh:442): no atomics, bitwise deterministic. The atomic variant is
+ * available as FA_B200_STAGE_FUSED (see fa_b200_backward_stages). */
 int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
                      const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
@@ -66,10 +68,16 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
 
 /* Stages of the backward, for fa_b200_backward_stages. */
 enum {
-  FA_B200_STAGE_ROWSUM = 1,  /* Dv = rowsum(dO o O) into the workspace */
+  FA_B200_STAGE_ROWSUM = 1,  /* Dv = rowsum(dO o O) into the workspace; also zeroes an
+                              * fp32 dq (the FUSED stage accumulates into it) */
   FA_B200_STAGE_DKDV = 2,    /* dK, dV (reads the workspace) */
   FA_B200_STAGE_DQ = 4,      /* dQ (reads the workspace) */
-  FA_B200_STAGE_ALL = 7
+  FA_B200_STAGE_ALL = 7,      /* ROWSUM | DKDV | DQ: the deterministic set */
+  FA_B200_STAGE_FUSED = 8     /* dK, dV and dQ in one kernel, dQ added with fp32 atomics
+                               * into a zeroed fp32 dq (the reference's scheme); needs
+                               * dq_fp32 and a prior ROWSUM stage (which zeroes dq);
+                               * excludes DKDV and DQ. Not bitwise deterministic, and on
+                               * B200 slower than DKDV + DQ: the atomics dominate */
 };
 
 /* fa_b200_backward restricted to the stages in `stages`. The dK/dV and dQ

@@ -62,7 +62,8 @@ def test_backward_argument_errors():
     need = _lib.lib().fa_b200_backward_workspace_bytes(1, 4, 16)
     assert bwd(ws_bytes=need - 4) == 7             # one float short
     assert bwd(ws=MISALIGNED) == 4
-    assert bwd(stages=8) == 3                       # unknown stage bit
+    assert bwd(stages=16) == 3                      # unknown stage bit
+    assert bwd(stages=8 | 2) == 3                   # FUSED excludes DKDV / DQ
 
 
 def test_workspace_size():

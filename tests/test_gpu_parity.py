@@ -78,16 +78,52 @@ def test_input_regimes(cuda, regime, D, causal):
         assert orc.rel(got, ref) < TOL
 
 
-def test_backward_op_contract(cuda):
+@pytest.mark.parametrize("D,causal", [(64, True), (128, False)])
+def test_backward_op_contract(cuda, D, causal):
     """fa_p100_ext.backward returns dq fp32 (B,Hq,N,D) and dk/dv fp16 (B,Hkv,N,D),
-    like fa_p100_ext.cu:121-123, and the fp32 dq rounds to the fp16 autograd dq."""
+    like fa_p100_ext.cu:121-123 (fused kernel, atomic dQ); the fp16-dq path (separate
+    kernels) agrees with it and is bitwise deterministic."""
     import fa_p100_ext
-    q, k, v, do = orc.seeded_inputs(2, 4, 2, 200, 64, seed=5)
+    q, k, v, do = orc.seeded_inputs(2, 4, 2, 200, D, seed=5)
     q, k, v, do = (t.to(cuda) for t in (q, k, v, do))
-    o, lse = fa_p100_ext.forward(q, k, v, True, False)
-    dq, dk, dv = fa_p100_ext.backward(q, k, v, do, o, lse, True)
+    o, lse = fa_p100_ext.forward(q, k, v, causal, False)
+    dq, dk, dv = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
     assert dq.dtype == torch.float32 and dq.shape == q.shape
     assert dk.dtype == torch.float16 and dk.shape == k.shape and dv.shape == v.shape
-    dq16, dk2, dv2 = fa_p100_ext.backward_into(q, k, v, do, o, lse, True, torch.float16)
-    assert torch.equal(dq.half(), dq16)
-    assert torch.equal(dk, dk2) and torch.equal(dv, dv2)   # deterministic
+    dq16, dk2, dv2 = fa_p100_ext.backward_into(q, k, v, do, o, lse, causal, torch.float16)
+    dq16b, dk3, dv3 = fa_p100_ext.backward_into(q, k, v, do, o, lse, causal, torch.float16)
+    assert torch.equal(dq16, dq16b) and torch.equal(dk2, dk3) and torch.equal(dv2, dv3)
+    for a, b in ((dq, dq16), (dk, dk2), (dv, dv2)):
+        assert orc.frob_rel(a, b) < 2e-3
+    rq, rk, rv = orc.attention_grads(q, k, v, do, causal)
+    for got, ref in ((dq, rq), (dk, rk), (dv, rv), (dq16, rq)):
+        assert orc.frob_rel(got, ref) < 1e-2
+
+
+@pytest.mark.parametrize("D,causal,Hq,Hkv,N", [(64, True, 4, 2, 333), (128, False, 8, 1, 700),
+                                               (128, True, 4, 4, 1024)])
+def test_fused_stage_matches(cuda, D, causal, Hq, Hkv, N):
+    """The opt-in fused stage (dK, dV, dQ in one kernel, dQ by fp32 atomics)
+    against the oracle and the default kernels."""
+    import _lib
+    import fa_p100_ext
+    q, k, v, do = (t.to(cuda) for t in orc.seeded_inputs(1, Hq, Hkv, N, D, seed=8))
+    o, lse = fa_p100_ext.forward(q, k, v, causal, False)
+    lib = _lib.lib()
+    dq = torch.empty(q.shape, device=cuda)
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    ws_b = lib.fa_b200_backward_workspace_bytes(1, Hq, N)
+    ws = torch.empty(ws_b // 4, device=cuda)
+    st = lib.fa_b200_backward_stages(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                     o.data_ptr(), lse.data_ptr(), dq.data_ptr(), 1, dk.data_ptr(),
+                                     dv.data_ptr(), ws.data_ptr(), ws_b, 1, Hq, Hkv, N, D,
+                                     int(causal), 1 | 8, torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "fused stage")
+    torch.cuda.synchronize()
+    assert _lib.device_error(0) == 0
+    rq, rk, rv = orc.attention_grads(q, k, v, do, causal)
+    for got, ref in ((dq, rq), (dk, rk), (dv, rv)):
+        assert orc.frob_rel(got, ref) < 1e-2
+    dq2, dk2, dv2 = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
+    assert torch.equal(dk, dk2) and torch.equal(dv, dv2)
+    assert orc.frob_rel(dq, dq2) < 1e-4
