@@ -166,17 +166,16 @@ __device__ __forceinline__ void tmem_st_pairs(uint32_t taddr, const float (&x)[2
 //   warp  8    TMEM allocation + MMA issue
 //   warp  9    TMA producer: K, V once; then Q_i (+ its LSE/Dv slices), dO_i
 // TMEM: S^T cols 0..127 | dP^T 128..255 | dV 256..256+D | dK 256+D..256+2D
-// P^T and dS^T (fp16 pairs) are written by the compute threads into TMEM
-// columns the same threads have already read: P^T over S^T cols 32..95, dS^T
-// over dP^T cols 160..223 (group w writes 32w+32.. / 32w+160.., inside its own
-// 64-column slice), and feed dV += P^T dO and dK += dS^T Q as the A operand
-// from TMEM. MMA order per step i (brackets = what it waits for):
-//   [P_i] dV_i ; [dS_i] dK_i ; [Q_{i+1}] S^T_{i+1} ; [dO_{i+1}] dP^T_{i+1}
-// S^T_{i+1} overwrites P_i and dP^T_{i+1} overwrites dS_i; each is issued
-// after the MMA that reads them, and the tensor core executes one CTA's MMAs
-// in issue order. Q_{i+1} reuses the ring slot Q_{i-1} frees after dK_{i-1},
-// so four MMA groups (~3000 cycles) separate that release from S^T_{i+1}:
-// enough to hide the TMA round trip.
+// P^T goes to a shared-memory tile [key][query] (the A operand of dV), so the
+// next S^T can overwrite S^T_i as soon as the compute threads have read it
+// and the tensor core works on S^T_{i+1} during the P phase. dS^T (fp16
+// pairs) is written into dP^T columns its threads have already read (cols
+// 160..223; group w writes 160+32w..) and feeds dK as the A operand from TMEM.
+// MMA order per step i (brackets = what it waits for):
+//   [S^T_i read, Q_{i+1}] S^T_{i+1} ; [P_i] dV_i ; [dS_i] dK_i ;
+//   [dO_{i+1}] dP^T_{i+1}
+// dP^T_{i+1} overwrites dS_i after dK_i has read it: the tensor core executes
+// one CTA's MMAs in issue order. P_{i+1} waits for dV_i (b_dv).
 // Every barrier's arrivals are gated on an MMA that needed all arrivals of the
 // previous phase, so no phase can receive arrivals from two steps.
 // ---------------------------------------------------------------------------
@@ -190,16 +189,17 @@ struct DkdvCfg {
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_RING = OFF_V + TILE;
-  static constexpr int OFF_LSE = OFF_RING + STAGES * TILE;   // [2][128] LSE*log2e, [2][128] Dv*scale
+  static constexpr int OFF_P = OFF_RING + STAGES * TILE;     // 128 keys x 128 queries fp16
+  static constexpr int OFF_LSE = OFF_P + 32768;              // [2][128] LSE*log2e, [2][128] Dv*scale
   static constexpr int OFF_BAR = OFF_LSE + 2048;
-  // kv, full[ST], empty[ST], s, dp, p, ds, fin
-  static constexpr int NBAR = 1 + 2 * STAGES + 5;
+  // kv, full[ST], empty[ST], s, dp, sfree, p, ds, dv, fin
+  static constexpr int NBAR = 1 + 2 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;   // window must start 1024-aligned
   static constexpr int THREADS = 320;
   static constexpr int NCOMPUTE = 256;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
-  static constexpr uint32_t COL_P = 32, COL_DS = 160;
+  static constexpr uint32_t COL_DS = 160;
 };
 
 template <int D>
@@ -212,11 +212,11 @@ __global__ void __launch_bounds__(320, 1)
   if (!smem_aligned_or_report(smem_raw, p.err)) return;
   const uint32_t sbase = smem_u32(smem_raw);
   const uint32_t s_k = sbase + C::OFF_K, s_v = sbase + C::OFF_V, s_ring = sbase + C::OFF_RING;
-  const uint32_t s_lse = sbase + C::OFF_LSE;
+  const uint32_t s_lse = sbase + C::OFF_LSE, s_p = sbase + C::OFF_P;
   const uint32_t b_kv = sbase + C::OFF_BAR;
   const uint32_t b_full = b_kv + 8, b_empty = b_full + 8 * C::STAGES;
-  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 8, b_p = b_dp + 8, b_ds = b_p + 8,
-                 b_fin = b_ds + 8;
+  const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 8, b_sfree = b_dp + 8,
+                 b_p = b_sfree + 8, b_ds = b_p + 8, b_dv = b_ds + 8, b_fin = b_dv + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -243,8 +243,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(b_s, 1);
     mbar_init(b_dp, 1);
+    mbar_init(b_sfree, C::NCOMPUTE);
     mbar_init(b_p, C::NCOMPUTE);
     mbar_init(b_ds, C::NCOMPUTE);
+    mbar_init(b_dv, 1);
     mbar_init(b_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -316,22 +318,22 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
       constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV, dK (A from TMEM)
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (SS), dK (TS)
       // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
+        const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_t,
-                 kk > 0 ? 1u : 0u);
+          mma_ss(d_tmem, sdesc_add(da, off), sdesc_add(db, off), id_t, kk > 0 ? 1u : 0u);
         }
       };
       // acc += (P or dS)^T (TMEM, 128 keys x 128 queries) * (dO or Q) (MN-major smem)
       auto issue_g = [&](uint32_t d_tmem, uint32_t a_tmem, uint32_t y_s, bool acc) {
+        const uint64_t dy = sdesc_sw128(y_s, 16384, 1024);
 #pragma unroll
         for (int kk = 0; kk < C::BM / 16; ++kk)
-          mma_ts(d_tmem, a_tmem + kk * 8, sdesc_sw128(y_s + kk * 2048, 16384, 1024), id_g,
-                 (acc || kk > 0) ? 1u : 0u);
+          mma_ts(d_tmem, a_tmem + kk * 8, sdesc_add(dy, kk * 2048), id_g, (acc || kk > 0) ? 1u : 0u);
       };
       auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
@@ -350,23 +352,32 @@ __global__ void __launch_bounds__(320, 1)
       for (int i = 0; i < total && ok; ++i) {
         const int it_q = 2 * i, it_do = 2 * i + 1;
         const bool more = i + 1 < total;
-        ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        issue_g(tmem + C::COL_DV, tmem + C::COL_P, slot_addr(it_do), i > 0);
-        mma_commit(b_empty + 8 * slot_of(it_do));
-        ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        issue_g(tmem + C::COL_DK, tmem + C::COL_DS, slot_addr(it_q), i > 0);
-        mma_commit(b_empty + 8 * slot_of(it_q));
-        if (more) {
-          ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
+        if (more) {  // S^T_{i+1} as soon as S^T_i has been read
+          ok = mbar_wait(b_sfree, i & 1, ctl, kErrTimeoutMma) &&
+               mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
           issue_t(tmem + C::COL_S, s_k, slot_addr(it_q + 2));
           mma_commit(b_s);
         }
+        ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);   // dV_i += P_i^T dO_i
+        if (!ok) break;
+        tc_fence_after();
+        {
+          const uint64_t dpt = sdesc_sw128(s_p, 16, 1024);
+          const uint64_t ddo = sdesc_sw128(slot_addr(it_do), 16384, 1024);
+#pragma unroll
+          for (int kk = 0; kk < C::BM / 16; ++kk)
+            mma_ss(tmem + C::COL_DV, sdesc_add(dpt, (kk >> 2) * 16384 + (kk & 3) * 32),
+                   sdesc_add(ddo, kk * 2048), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(b_dv);
+        mma_commit(b_empty + 8 * slot_of(it_do));
+        ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);  // dK_i += dS_i^T Q_i
+        if (!ok) break;
+        tc_fence_after();
+        issue_g(tmem + C::COL_DK, tmem + C::COL_DS, slot_addr(it_q), i > 0);
+        mma_commit(b_empty + 8 * slot_of(it_q));
         if (more) {
           ok = mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
           if (!ok) break;
@@ -408,6 +419,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      tc_fence_before();
+      mbar_arrive(b_sfree);   // S^T_i is in registers: S^T_{i+1} may overwrite it
       // this step's 64 LSE / Dv values for the group, read as 16-byte vectors
       // (a broadcast LDS per value would cost 8 warps x 64 issue slots on the
       // shared-memory pipe per phase)
@@ -439,8 +452,14 @@ __global__ void __launch_bounds__(320, 1)
             if (q < qlim || q >= p.n) pv[h][c] = 0.f;
           }
       }
-      tmem_st_pairs(tmem + C::COL_P + 32 * w + lane_off, pv);
-      tmem_st_wait();
+      if (i > 0) {  // dV_{i-1} has finished reading P_{i-1} from the tile
+        ok = mbar_wait(b_dv, (i - 1) & 1, ctl, kErrTimeoutSoftmax);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+      st_row32_sw128(s_p + w * 16384, r, 0, pv[0]);
+      st_row32_sw128(s_p + w * 16384, r, 1, pv[1]);
+      fence_async_smem();
       tc_fence_before();
       mbar_arrive(b_p);
 
@@ -661,11 +680,11 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t id_s = idesc_f16(128, 128, false, false);
       constexpr uint32_t id_q = idesc_f16(128, D, false, true);
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
+        const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_s,
-                 kk > 0 ? 1u : 0u);
+          mma_ss(d_tmem, sdesc_add(da, off), sdesc_add(db, off), id_s, kk > 0 ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(b_qdo, 0, ctl, kErrTimeoutMma);
@@ -702,10 +721,11 @@ __global__ void __launch_bounds__(320, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t ds_t = tmem + C::COL_DS + 64 * (j & 1);
+        const uint64_t dkb = sdesc_sw128(k_addr(j), 16384, 1024);
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk)
-          mma_ts(tmem + C::COL_DQ, ds_t + kk * 8, sdesc_sw128(k_addr(j) + kk * 2048, 16384, 1024),
-                 id_q, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::COL_DQ, ds_t + kk * 8, sdesc_add(dkb, kk * 2048), id_q,
+                 (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(kempty(j));  // K_j no longer needed
       }
       mma_commit(b_fin);
@@ -977,11 +997,11 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (TS), dK (SS)
       constexpr uint32_t id_q = idesc_f16(128, D, true, true);      // dQ: A = dS MN-major
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
+        const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          mma_ss(d_tmem, sdesc_sw128(a_s + off, 16, 1024), sdesc_sw128(b_s_ + off, 16, 1024), id_t,
-                 kk > 0 ? 1u : 0u);
+          mma_ss(d_tmem, sdesc_add(da, off), sdesc_add(db, off), id_t, kk > 0 ? 1u : 0u);
         }
       };
       auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };

@@ -72,11 +72,11 @@ namespace fab {
 template <int D>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t k_s) {
   constexpr uint32_t idesc = idesc_f16(128, 128, false, false);
+  const uint64_t dq = sdesc_sw128(q_s, 16, 1024), dk = sdesc_sw128(k_s, 16, 1024);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-    mma_ss(d_tmem, sdesc_sw128(q_s + off, 16, 1024), sdesc_sw128(k_s + off, 16, 1024), idesc,
-           kk > 0 ? 1u : 0u);
+    mma_ss(d_tmem, sdesc_add(dq, off), sdesc_add(dk, off), idesc, kk > 0 ? 1u : 0u);
   }
 }
 // O[tmem] (+)= P (128 x 128 keys, K-major) * V (128 keys x D, MN-major)
@@ -84,11 +84,12 @@ template <int D>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_s, uint32_t v_s,
                                          bool accumulate) {
   constexpr uint32_t idesc = idesc_f16(128, D, false, true);
+  const uint64_t dp = sdesc_sw128(p_s, 16, 1024), dv = sdesc_sw128(v_s, 16384, 1024);
 #pragma unroll
   for (int kk = 0; kk < 128 / 16; ++kk) {
     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-    mma_ss(d_tmem, sdesc_sw128(p_s + aoff, 16, 1024), sdesc_sw128(v_s + kk * 2048, 16384, 1024),
-           idesc, (accumulate || kk > 0) ? 1u : 0u);
+    mma_ss(d_tmem, sdesc_add(dp, aoff), sdesc_add(dv, kk * 2048), idesc,
+           (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 

@@ -208,6 +208,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// The descriptor of the same tile `byte_off` bytes further on. The start
+// address is the low 14-bit field (address >> 4); shared-memory addresses stay
+// below 256 KiB, so the addition never carries into the next field.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_off) {
+  return desc + (byte_off >> 4);
+}
+
 // Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulation.
 // a_mn / b_mn select MN-major (transposed) operands.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn) {
