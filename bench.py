@@ -230,22 +230,23 @@ def run_reference(args, world, rank):
 # GPU side: our kernels
 # ---------------------------------------------------------------------------
 STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ, STAGE_FUSED = 1, 2, 4, 8
-KERNELS = ("fwd", "bwd_rowsum", "bwd_dkdv", "bwd_dq")
+# The default backward for the reference's contract (fp32 dq): the row-sum
+# preprocess (which also zeroes dq) and the fused dK/dV/dQ kernel.
+KERNELS = ("fwd", "bwd_rowsum", "bwd_fused")
+STAGES = (STAGE_ROWSUM, STAGE_FUSED)
 
 
 def kernel_work(name, B, Hq, Hkv, N, D, causal):
     """Algorithmic work of one launch: (amount, unit, bound).
-    fwd: the forward's 2 contractions; dkdv: 4 of the backward's 5 (S recompute,
-    dP, dV, dK); dq: the dQ contraction only (its S/dP recompute is not counted);
-    rowsum: bytes of O and dO read plus Dv written."""
+    fwd: the forward's 2 contractions; fused: the backward's 5 (S recompute,
+    dP, dV, dK, dQ); rowsum: bytes of O and dO read, Dv and LSE*log2e written,
+    and the fp32 dq zeroed."""
     ff = flops_fwd(B, Hq, N, D, causal)
     if name == "fwd":
         return ff, "TFLOP/s", "tensor"
-    if name == "bwd_dkdv":
-        return 2.0 * ff, "TFLOP/s", "tensor"
-    if name == "bwd_dq":
-        return 0.5 * ff, "TFLOP/s", "tensor"
-    return 2.0 * B * Hq * N * D * 2 + B * Hq * N * 4, "GB/s", "hbm"
+    if name == "bwd_fused":
+        return 2.5 * ff, "TFLOP/s", "tensor"
+    return 2.0 * B * Hq * N * D * 2 + 2 * B * Hq * N * 4 + B * Hq * N * D * 4, "GB/s", "hbm"
 
 
 def qwen3_step_ms(dev, attn, steps, warmup, seq=8192):
@@ -312,7 +313,7 @@ def run_ours(args, world, rank, local):
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
     o = torch.empty_like(q)
     lse = torch.empty(B, Hq, N, device=dev)
-    dq = torch.empty_like(q)
+    dq = torch.empty(q.shape, device=dev, dtype=torch.float32)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     ws_bytes = lib.fa_b200_backward_workspace_bytes(B, Hq, N)
@@ -326,22 +327,23 @@ def run_ours(args, world, rank, local):
     def bwd_stage(mask):
         return lib.fa_b200_backward_stages(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), o.data_ptr(),
-            lse.data_ptr(), dq.data_ptr(), 0, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
+            lse.data_ptr(), dq.data_ptr(), 1, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
             ws_bytes, B, Hq, Hkv, N, D, int(causal), mask, sp)
 
     def step(record):
-        marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if record else None
+        nk = len(KERNELS)
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] if record else None
         if record:
             marks[0].record(stream)
         st = lib.fa_b200_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                                  lse.data_ptr(), B, Hq, Hkv, N, D, int(causal), 0, sp)
         _lib.check(st, "fa_b200_forward")
-        for i, mask in enumerate((STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ)):
+        for i, mask in enumerate(STAGES):
             if record:
                 marks[i + 1].record(stream)
             _lib.check(bwd_stage(mask), "fa_b200_backward_stages")
         if record:
-            marks[4].record(stream)
+            marks[nk].record(stream)
             step_ev.append(marks)
 
     for _ in range(args.warmup):
@@ -360,14 +362,14 @@ def run_ours(args, world, rank, local):
             step(True)
         torch.cuda.synchronize(dev)
         barrier(world)
-    launches = 4 * args.steps
+    launches = len(KERNELS) * args.steps
 
     per_kernel = {n: 0.0 for n in KERNELS}
     total_ms = 0.0
     for m in step_ev:
         for i, n in enumerate(KERNELS):
             per_kernel[n] += m[i].elapsed_time(m[i + 1])
-        total_ms += m[0].elapsed_time(m[4])
+        total_ms += m[0].elapsed_time(m[len(KERNELS)])
     ms = total_ms / args.steps
     ms = max_over_ranks(ms, world, dev)
     per_kernel = {n: t / args.steps for n, t in per_kernel.items()}
@@ -399,7 +401,7 @@ def run_ours(args, world, rank, local):
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
     barrier(world)
-    launches += 4 * args.steps
+    launches += 3 * args.steps   # forward, row-sum, fused backward
     e2e_ms = max_over_ranks(e2e_ms / args.steps, world, dev)
     del dq_d
     if _lib.device_error(local) != 0:
@@ -525,7 +527,8 @@ def run_ring(args, world, rank, local):
                    "causal": causal, "parallelism": f"ring context parallel, zigzag x{world}"
                    if world > 1 else "single GPU",
                    "l2": "flushed (256 MiB write) before each step"},
-        "gpu_launches": args.steps * (pieces_fwd + 3 * pieces_fwd) if world > 1 else 4 * args.steps,
+        # each piece: one forward launch, and a row-sum + fused backward launch
+        "gpu_launches": args.steps * 3 * pieces_fwd if world > 1 else 3 * args.steps,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -143,14 +143,13 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Both dq dtypes take the separate dK/dV and dQ kernels: no atomics, bitwise
-// deterministic, and on B200 faster than the fused kernel, whose per-step
-// fp32 atomic adds of dQ (4.4 GB at B=1, H=32, N=8192) cost more than the
-// dQ kernel's recompute (measured: fused 2.32 ms, of which 0.85 ms is the
-// atomics, against 1.95 ms for dK/dV + dQ).
+// An fp32 dQ is produced by the fused kernel: one pass, dQ added into the
+// zeroed output by TMA reduce-adds (the reference's fp32 dQ contract, and like
+// its atomicAdd not bitwise deterministic). An fp16 dQ has no fp32 buffer to
+// add into and takes the separate dK/dV and dQ kernels, which own every output
+// row outright and are bitwise deterministic.
 int default_stages(int dq_fp32) {
-  (void)dq_fp32;
-  return FA_B200_STAGE_ALL;
+  return dq_fp32 ? (FA_B200_STAGE_ROWSUM | FA_B200_STAGE_FUSED) : FA_B200_STAGE_ALL;
 }
 
 // Device address of g_noalloc_scratch on `dev`, looked up once per device with
@@ -250,8 +249,12 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_FUSED) {
+    // dQ (fp32) as 32-row x 32-column boxes for the TMA reduce-adds
+    CUtensorMap tdq;
+    if (!make_map(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, BH, 32))
+      return FA_B200_ERR_TENSOR_MAP;
     bwd_fused_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), FusedCfg<D>::THREADS,
-                          FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
+                          FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }
   if (stages & FA_B200_STAGE_DQ) {

@@ -833,47 +833,59 @@ __global__ void __launch_bounds__(320, 1)
 
 }  // namespace fab
 
+
 namespace fab {
 
 // ---------------------------------------------------------------------------
-// Fused dK / dV / dQ: the dK/dV kernel's CTA (128 keys, looping over the GQA
-// group and the query blocks), which also forms each step's dQ contribution
-// dQ_i = scale dS_i K and adds it into a zeroed fp32 dQ with vector atomic
-// adds -- the reference's scheme (flash_bwd.cuh:378-444), without recomputing
-// S and dP in a second kernel. Used when the caller takes dQ in fp32.
+// Fused dK / dV / dQ in one pass: the key-stationary CTA of the dK/dV kernel
+// (128 keys, looping over the GQA group and the query blocks) also forms each
+// step's dQ contribution dQ_i = dS_i K and adds it into a zeroed fp32 dQ, as
+// the reference does with atomicAdd (flash_bwd.cuh:378-444) -- but with no
+// recompute of S and dP in a second kernel, and the adds done by the TMA unit:
+// each warp stages its 32 query rows x 32 columns of dQ_i (a 4 KiB swizzled
+// box) in shared memory and issues one tiled reduce-add of the box into global
+// memory, so the adds are coalesced 128-byte rows and run asynchronously.
+// The add order varies from run to run, so dQ is not bitwise deterministic.
 //   warps 0-7  compute: two warpgroups; thread r is key row r for P and dS and
-//              query row r when it reads dQ_i out
+//              query row r of dQ_i; group w owns queries (and dQ columns)
+//              64w.. of each step
 //   warp  8    TMEM allocation + MMA issue
-//   warp  9    TMA producer (as in bwd_dkdv_kernel)
-// TMEM: S^T 0..127 (P^T fp16 pairs over cols 32..95) | dP^T 128..255, then
-//       dQ_i once dS_i is formed | dV 256.. | dK 256+D..
-// Shared: K, V, 4-slot Q/dO ring, LSE/Dv slices [2], one dS^T tile [key][query].
-// MMA order per step i:
-//   [P_i] dV += P^T dO (A = P^T in TMEM) ; [dS_i] dK += dS^T Q (A = dS^T tile,
-//   K-major) ; dQ_i = dS K into the dP^T columns (A = the same tile read
-//   MN-major, B = K MN-major) ; [Q_{i+1}] S^T_{i+1} ; [dQ_i read] dP^T_{i+1}
+//   warp  9    TMA producer: K, V once; then Q_i (+ LSE/Dv slices), dO_i
+// TMEM: S^T 0..127, with P^T (fp16 pairs) written back over cols 32..95 |
+//       dP^T 128..255, then dQ_i once dS_i has been formed | dV 256.. | dK 256+D..
+// Shared: K, V, a 3-slot Q/dO ring, the dS^T tile [key][query], eight 4 KiB
+// dQ staging boxes (one per compute warp; with D = 128 a warp's second box is
+// staged in its own rows of the dS tile), LSE/Dv slices for two steps.
+// MMA order per step i (brackets = what it waits for):
+//   [P_i] dV_i = P^T dO (A in TMEM) ; [Q_{i+1}] S^T_{i+1} ;
+//   [dS_i] dK_i = dS^T Q (A = the dS tile K-major), dQ_i = dS K (A = the same
+//   tile MN-major, into the dP^T columns) ; [dQ_i read, dO_{i+1}] dP^T_{i+1}
+// and the compute warps run dS_i, P_{i+1}, dQ_i read-out, so that the P phase
+// of the next step overlaps dK_i and dQ_i on the tensor core.
 // Overwrites follow issue order (S^T_{i+1} after dV_i read P_i; dQ_i after
-// the compute threads read dP_i; dP^T_{i+1} after they read dQ_i out). The dS
-// tile is rewritten at step i+1 only after this thread saw dQ_i complete.
+// the compute threads read dP_i; dP^T_{i+1} after they read dQ_i). The dS
+// tile is rewritten for step i+1 only after dP^T_{i+1} completed, which was
+// issued after dK_i and dQ_i. The Q slot of step i is released after dK_i and
+// the producer fills the ring in order, so the LSE/Dv slice buffer i & 1 is
+// reloaded (for step i+2) only after every compute thread finished step i.
 // ---------------------------------------------------------------------------
-#ifndef FAB_DQ_RED
-#define FAB_DQ_RED red_add_v4
-#endif
-
 template <int D>
 struct FusedCfg {
   static constexpr int BN = 128, BM = 128, CH = D / 64;
   static constexpr int TILE = 128 * D * 2;
-  static constexpr int STAGES = 4;
+  static constexpr int STAGES = (D == 64) ? 4 : 3;   // 3 or 4 keep the slice buffers safe
+  static_assert(STAGES == 3 || STAGES == 4, "slice-buffer reuse assumes a 3- or 4-slot ring");
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_RING = OFF_V + TILE;
   static constexpr int OFF_DS = OFF_RING + STAGES * TILE;    // 128 keys x 128 queries fp16
-  static constexpr int OFF_LSE = OFF_DS + 32768;             // [2][128] LSE*log2e, [2][128] Dv*scale
+  static constexpr int OFF_STG = OFF_DS + 32768;             // 8 x (32 rows x 32 fp32)
+  static constexpr int OFF_LSE = OFF_STG + 8 * 4096;         // [2][128] LSE*log2e, [2][128] Dv*scale
   static constexpr int OFF_BAR = OFF_LSE + 2048;
   // kv, full[ST], empty[ST], s, dp, p, ds, dqfull, dqfree, fin
   static constexpr int NBAR = 1 + 2 * STAGES + 7;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;     // window must start 1024-aligned
+  static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 320;
   static constexpr int NCOMPUTE = 256;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -885,7 +897,7 @@ template <int D>
 __global__ void __launch_bounds__(320, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const BwdParams p) {
+                     const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
   using C = FusedCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (!smem_aligned_or_report(smem_raw, p.err)) return;
@@ -900,15 +912,18 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // grid (B*Hkv, key blocks): causal key block 0 has the most work and goes
+  // first. CTAs that run together start at neighbouring query blocks and
+  // advance in step, so the Q/dO tiles and dQ rows they share stay in L2.
   const int bkv = blockIdx.x;
   const int kvb = blockIdx.y;
   const int hkv = p.hq / p.group;
   const int b = bkv / hkv, kvh = bkv % hkv;
   const int kv0 = kvb * C::BN;
   const int nqb = (p.n + C::BM - 1) / C::BM;
-  const int i_start = p.causal ? kvb : 0;
+  const int i_start = p.causal ? kvb : 0;   // BM == BN: the diagonal block
   const int nq_head = nqb - i_start;
-  const int total = p.group * nq_head;
+  const int total = p.group * nq_head;      // (group head, query block) steps
   const Ctl ctl{abort_flag, p.err};
   auto slot_of = [](int it) { return it % C::STAGES; };
   auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
@@ -950,7 +965,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       int it = 0;
       bool ok = true;
-      constexpr int kAhead = 2;
+      constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
       auto prefetch_step = [&](int st) {
         const int q0p = (i_start + st % nq_head) * C::BM;
         const int bhp = b * p.hq + kvh * p.group + st / nq_head;
@@ -996,6 +1011,7 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
       constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (TS), dK (SS)
       constexpr uint32_t id_q = idesc_f16(128, D, true, true);      // dQ: A = dS MN-major
+      // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
         const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
 #pragma unroll
@@ -1005,6 +1021,9 @@ __global__ void __launch_bounds__(320, 1)
         }
       };
       auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
+      const uint64_t d_dsk = sdesc_sw128(s_ds, 16, 1024);       // dS^T tile as K-major A
+      const uint64_t d_dsm = sdesc_sw128(s_ds, 16384, 1024);    // dS tile as MN-major A
+      const uint64_t d_kmn = sdesc_sw128(s_k, 16384, 1024);     // K as MN-major B
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
       if (ok) ok = mbar_wait(b_full + 8 * slot_of(0), ph_of(0), ctl, kErrTimeoutMma);
       if (ok) {
@@ -1025,33 +1044,40 @@ __global__ void __launch_bounds__(320, 1)
         ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
+        {
+          const uint64_t ddo = sdesc_sw128(slot_addr(it_do), 16384, 1024);
 #pragma unroll
-        for (int kk = 0; kk < C::BM / 16; ++kk)
-          mma_ts(tmem + C::COL_DV, tmem + C::COL_P + kk * 8,
-                 sdesc_sw128(slot_addr(it_do) + kk * 2048, 16384, 1024), id_g,
-                 (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < C::BM / 16; ++kk)
+            mma_ts(tmem + C::COL_DV, tmem + C::COL_P + kk * 8, sdesc_add(ddo, kk * 2048), id_g,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+        }
         mma_commit(b_empty + 8 * slot_of(it_do));
-        // dK_i += dS_i^T Q_i ; dQ_i = dS_i K
-        ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < C::BM / 16; ++kk)
-          mma_ss(tmem + C::COL_DK, sdesc_sw128(s_ds + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                 sdesc_sw128(slot_addr(it_q) + kk * 2048, 16384, 1024), id_g,
-                 (i > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(b_empty + 8 * slot_of(it_q));
-#pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk)
-          mma_ss(tmem + C::COL_DQ, sdesc_sw128(s_ds + kk * 2048, 16384, 1024),
-                 sdesc_sw128(s_k + kk * 2048, 16384, 1024), id_q, kk > 0 ? 1u : 0u);
-        mma_commit(b_dqfull);
+        // S^T_{i+1}: its P phase overlaps dK_i and dQ_i
         if (more) {
           ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
           issue_t(tmem + C::COL_S, s_k, slot_addr(it_q + 2));
           mma_commit(b_s);
+        }
+        // dK_i += dS_i^T Q_i ; dQ_i = dS_i K
+        ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        {
+          const uint64_t dq_mn = sdesc_sw128(slot_addr(it_q), 16384, 1024);
+#pragma unroll
+          for (int kk = 0; kk < C::BM / 16; ++kk)
+            mma_ss(tmem + C::COL_DK, sdesc_add(d_dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
+                   sdesc_add(dq_mn, kk * 2048), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(b_empty + 8 * slot_of(it_q));
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          mma_ss(tmem + C::COL_DQ, sdesc_add(d_dsm, kk * 2048), sdesc_add(d_kmn, kk * 2048), id_q,
+                 kk > 0 ? 1u : 0u);
+        mma_commit(b_dqfull);
+        if (more) {
           ok = mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma) &&
                mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
           if (!ok) break;
@@ -1067,27 +1093,25 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ compute (warps 0-7)
-    const int w = warp >> 2;
-    const int r = threadIdx.x & 127;
+    const int w = warp >> 2;            // query half of each step
+    const int r = threadIdx.x & 127;    // key row within the block
     const int kvrow = kv0 + r;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const int qlim = p.causal ? kvrow : -1;
-    float* dq = static_cast<float*>(p.dq);
-    bool ok = true;
-    for (int i = 0; i < total; ++i) {
-      const int qb0 = (i_start + i % nq_head) * C::BM;   // query block start
-      const int q0 = qb0 + 64 * w;                         // this group's 64 queries
-      const int bh = b * p.hq + kvh * p.group + i / nq_head;
+    const int qlim = p.causal ? kvrow : -1;  // a query column is live iff qlim <= q < N
+    const uint32_t stg = sbase + C::OFF_STG + warp * 4096;   // this warp's dQ box
+    uint32_t sr[2][32];
+    float pv[2][32];
+
+    // P_i^T = exp2(S^T * scale*log2e - LSE*log2e), written over S^T in TMEM
+    auto phase_p = [&](int i) -> bool {
+      const int q0 = (i_start + i % nq_head) * C::BM + 64 * w;
       const int it_q = 2 * i;
-      const uint32_t ph = i & 1;
       const bool need_mask = (q0 + 64 > p.n) || (p.causal && q0 < kv0 + 127);
-      // ---- P phase
-      ok = mbar_wait(b_full + 8 * slot_of(it_q), ph_of(it_q), ctl, kErrTimeoutSoftmax) &&
-           mbar_wait(b_s, ph, ctl, kErrTimeoutSoftmax);
+      bool ok = mbar_wait(b_full + 8 * slot_of(it_q), ph_of(it_q), ctl, kErrTimeoutSoftmax) &&
+                mbar_wait(b_s, i & 1, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+      if (!ok) return false;
       tc_fence_after();
-      uint32_t sr[2][32];
       tmem_ld32(tmem + C::COL_S + 64 * w + lane_off, sr[0]);
       tmem_ld32(tmem + C::COL_S + 64 * w + 32 + lane_off, sr[1]);
       tmem_ld_wait_only();
@@ -1097,8 +1121,6 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
       const float4* lse4 =
           reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4;
-      const float4* dvs4 = lse4 + 64;
-      float pv[2][32];
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -1106,8 +1128,10 @@ __global__ void __launch_bounds__(320, 1)
           const float4 l4 = lse4[8 * h + c4];
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4)
-            pv[h][4 * c4 + e4] = ex2(fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale_log2, -lv[e4]));
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const int c = 4 * c4 + e4;
+            pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lv[e4]));
+          }
         }
       if (need_mask) {
 #pragma unroll
@@ -1122,10 +1146,14 @@ __global__ void __launch_bounds__(320, 1)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p);
-      // ---- dS phase
-      ok = mbar_wait(b_dp, ph, ctl, kErrTimeoutSoftmax);
+      return true;
+    };
+
+    // dS_i^T = P^T o (dP^T * scale - Dv*scale), into the shared [key][query] tile
+    auto phase_ds = [&](int i) -> bool {
+      bool ok = mbar_wait(b_dp, i & 1, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+      if (!ok) return false;
       tc_fence_after();
       tmem_ld32(tmem + C::COL_DP + 64 * w + lane_off, sr[0]);
       tmem_ld32(tmem + C::COL_DP + 64 * w + 32 + lane_off, sr[1]);
@@ -1134,6 +1162,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
+      const float4* dvs4 =
+          reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4 + 64;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -1144,41 +1174,76 @@ __global__ void __launch_bounds__(320, 1)
           for (int e4 = 0; e4 < 4; ++e4)
             pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, -dv[e4]);
         }
-      // dS^T row r (this group's 64 queries) into the swizzled [key][query] tile
-      const uint32_t my_tile = s_ds + w * 16384;
-      st_row32_sw128(my_tile, r, 0, pv[0]);
-      st_row32_sw128(my_tile, r, 1, pv[1]);
+      if constexpr (D / 64 > 1) {   // this warp's rows of the tile staged a dQ box
+        if (lane == 0) bulk_wait_read_all_but_last();   // committed before box 0
+        __syncwarp();
+      }
+      st_row32_sw128(s_ds + w * 16384, r, 0, pv[0]);
+      st_row32_sw128(s_ds + w * 16384, r, 1, pv[1]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(b_ds);
-      // ---- dQ read-out: lane r of dQ_i is query qb0 + r; this group takes
-      // dQ columns w*D/2 .. (w+1)*D/2 - 1 and adds them into the fp32 dQ
-      ok = mbar_wait(b_dqfull, ph, ctl, kErrTimeoutSoftmax);
+      return true;
+    };
+
+    // dQ_i read-out: TMEM lane r is query row qb0 + r; group w takes dQ
+    // columns w*D/2 .. +D/2, in boxes of 32 rows x 32 columns, each staged in
+    // shared memory and added into global dQ by the TMA unit. Box 0 goes to
+    // this warp's staging buffer; box 1 (D = 128) to the warp's own 4 KiB of
+    // the dS tile -- its 32 rows of one query half, which dK_i and dQ_i have
+    // finished reading and which the warp rewrites only in its next dS phase,
+    // after waiting for the TMA to have read the box. Box 1 is issued and
+    // committed first, so that wait does not include box 0.
+    auto phase_ro = [&](int i) -> bool {
+      const int qb0 = (i_start + i % nq_head) * C::BM;
+      const int bh = b * p.hq + kvh * p.group + i / nq_head;
+      bool ok = mbar_wait(b_dqfull, i & 1, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
+      if (!ok) return false;
       tc_fence_after();
-      constexpr int NCH = D / 64;   // 32-column chunks per group
+      constexpr int NB = D / 64;   // 32-column boxes per group
 #pragma unroll
-      for (int h = 0; h < NCH; ++h) tmem_ld32(tmem + C::COL_DQ + w * (D / 2) + 32 * h + lane_off, sr[h]);
+      for (int h = 0; h < NB; ++h)
+        tmem_ld32(tmem + C::COL_DQ + w * (D / 2) + 32 * h + lane_off, sr[h]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int h = 0; h < NCH; ++h)
+      for (int h = 0; h < NB; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
       tc_fence_before();
-      mbar_arrive(b_dqfree);
-      const int qrow = qb0 + r;
-      if (qrow < p.n) {
-        float* dst = dq + (static_cast<size_t>(bh) * p.n + qrow) * D + w * (D / 2);
+      mbar_arrive(b_dqfree);      // dP^T_{i+1} may overwrite the dQ_i columns
+      const int row0 = qb0 + 32 * (warp & 3);
+      if (lane == 0) bulk_wait_read_all();     // last step's box 0 has left the buffer
+      __syncwarp();
 #pragma unroll
-        for (int h = 0; h < NCH; ++h)
+      for (int h = 0; h < NB; ++h) {
+        const uint32_t box = h == 0 ? stg : s_ds + w * 16384 + (warp & 3) * 4096;
 #pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4)
-            FAB_DQ_RED(dst + 32 * h + 4 * c4, __uint_as_float(sr[h][4 * c4]),
-                       __uint_as_float(sr[h][4 * c4 + 1]), __uint_as_float(sr[h][4 * c4 + 2]),
-                       __uint_as_float(sr[h][4 * c4 + 3]));
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(box + lane * 128 + ((c ^ (lane & 7)) << 4), sr[h][4 * c], sr[h][4 * c + 1],
+                       sr[h][4 * c + 2], sr[h][4 * c + 3]);
       }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < p.n) {
+#pragma unroll
+        for (int h = NB - 1; h >= 0; --h) {
+          tma_reduce_add_3d(&tm_dq, h == 0 ? stg : s_ds + w * 16384 + (warp & 3) * 4096,
+                            w * (D / 2) + 32 * h, row0, bh);
+          bulk_commit_group();
+        }
+      }
+      return true;
+    };
+
+    bool ok = true;
+    if (total > 0) ok = phase_p(0);
+    for (int i = 0; i < total && ok; ++i) {
+      ok = phase_ds(i);
+      if (ok && i + 1 < total) ok = phase_p(i + 1);
+      if (ok) ok = phase_ro(i);
     }
+    if (lane == 0) bulk_wait_all();   // every dQ box added before the CTA exits
     if (ok && total > 0) {
       ok = mbar_wait(b_fin, 0, ctl, kErrTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok);

@@ -10,8 +10,10 @@ SIMT kernels replaced by tcgen05 tensor-core kernels in libfa_b200.so.
 D is 64 or 128, N is arbitrary, Hq a multiple of Hkv (MHA, GQA, MQA).
 `full_precision` is accepted and ignored: the tensor cores multiply fp16
 exactly and accumulate in fp32, which is the reference's fp32-MAC tier.
-The backward is deterministic: dQ comes from its own kernel rather than
-from the reference's fp32 atomics.
+The backward follows the reference's flow: dq in fp32 (accumulated across key
+blocks by TMA reduce-adds, so, like the reference's atomicAdd, not bitwise
+deterministic), then cast to q's dtype. fa_p100_ext.backward_into with an fp16
+dq takes the deterministic two-kernel backward instead.
 """
 import math
 
@@ -33,12 +35,8 @@ class _FlashAttnP100(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_o):
         q, k, v, o, lse = ctx.saved_tensors
-        # The reference returns dq in fp32 and casts it (fa_p100.py:45); the
-        # kernel rounds its fp32 accumulator straight to q's dtype instead,
-        # which is the same rounding without the intermediate tensor.
-        dq_dtype = torch.float16 if q.dtype == torch.float16 else torch.float32
-        dq, dk, dv = _ext.backward_into(q, k, v, grad_o.contiguous(), o, lse, ctx.causal,
-                                        dq_dtype)
+        # dq comes back in fp32 and is cast to q's dtype (fa_p100.py:43-45)
+        dq, dk, dv = _ext.backward(q, k, v, grad_o.contiguous(), o, lse, ctx.causal)
         return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
 
 

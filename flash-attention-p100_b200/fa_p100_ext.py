@@ -68,7 +68,9 @@ def forward(q, k, v, causal, full_precision=False):
 
 
 def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32):
-    """dq (dq_dtype), dk, dv. `dq_dtype` fp16 lets autograd skip the fp32 copy."""
+    """dq (dq_dtype), dk, dv. fp32 dq (the default, and `backward`) runs the
+    fused one-pass backward, whose dq adds are not bitwise deterministic; fp16
+    dq runs the two-kernel backward (dK/dV, then dQ), which is."""
     _check_in(q, "q")
     _check_in(dO, "dO")
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
