@@ -14,15 +14,20 @@
 //   warp  8    TMEM allocation + the single thread that issues tcgen05.mma
 //   warp  9    the single thread that issues TMA loads
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
-// Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate), P0, P1.
+// P_t (fp16 pairs, column c = keys 2c, 2c+1) is written back over the first 64
+// columns of S_t: each softmax thread owns its row's TMEM lane and has the
+// whole S row in registers by then. O_t += P_t V_j reads P_t from TMEM, so
+// P never touches shared memory, and V is the MMA's only shared operand.
+// Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate).
 //
 // Per key block j the MMA thread issues, in order,
 //   PV0_{j-1}... S0_j = Q0 K_j^T ; S1_j = Q1 K_j^T ; [P0_j] O0 += P0_j V_j ;
 //   S0_{j+1} ; [P1_j] O1 += P1_j V_j ; S1_{j+1} ; ...
 // so the tensor core computes one tile's S while the other tile's softmax runs.
-// tcgen05.commit tracks every MMA issued before it, so when softmax t sees
-// S_t,j+1 complete, PV_t,j is complete too: P_t's buffer and O_t are free to
-// rewrite, and no extra barrier is needed for either.
+// The tensor core executes one CTA's MMAs in issue order, so S_t,j+1 overwrites
+// P_t,j only after O_t += P_t,j V_j has read it; and tcgen05.commit tracks
+// every MMA issued before it, so when softmax t sees S_t,j+1 complete, PV_t,j is
+// complete too and O_t is free to rescale.
 #pragma once
 #include "sm100.cuh"
 
@@ -47,15 +52,14 @@ struct FwdCfg {
   static constexpr int CH = D / 64;             // 64-column chunks per row
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int KVBYTES = BN * D * 2;
-  static constexpr int PBYTES = BM * BN * 2;
-  static constexpr int STAGES = (D == 128) ? 3 : 6;
+  static constexpr int STAGES = (D == 128) ? 5 : 8;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
-  static constexpr int OFF_P = OFF_RING + STAGES * KVBYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * PBYTES;
+  static constexpr int OFF_BAR = OFF_RING + STAGES * KVBYTES;
   // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin; then tmem addr + abort flag
   static constexpr int NBAR = 1 + 2 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
+  static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 320;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O0 = 256, COL_O1 = 256 + D;
@@ -79,18 +83,16 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t
     mma_ss(d_tmem, sdesc_add(dq, off), sdesc_add(dk, off), idesc, kk > 0 ? 1u : 0u);
   }
 }
-// O[tmem] (+)= P (128 x 128 keys, K-major) * V (128 keys x D, MN-major)
+// O[tmem] (+)= P (128 x 128 keys, fp16 pairs in TMEM) * V (128 keys x D, MN-major)
 template <int D>
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_s, uint32_t v_s,
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_s,
                                          bool accumulate) {
   constexpr uint32_t idesc = idesc_f16(128, D, false, true);
-  const uint64_t dp = sdesc_sw128(p_s, 16, 1024), dv = sdesc_sw128(v_s, 16384, 1024);
+  const uint64_t dv = sdesc_sw128(v_s, 16384, 1024);
 #pragma unroll
-  for (int kk = 0; kk < 128 / 16; ++kk) {
-    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-    mma_ss(d_tmem, sdesc_add(dp, aoff), sdesc_add(dv, kk * 2048), idesc,
+  for (int kk = 0; kk < 128 / 16; ++kk)
+    mma_ts(d_tmem, p_tmem + kk * 8, sdesc_add(dv, kk * 2048), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
-  }
 }
 
 template <int D>
@@ -104,7 +106,6 @@ __global__ void __launch_bounds__(320, 1)
 
   const uint32_t s_q0 = sbase + C::OFF_Q, s_q1 = s_q0 + C::QBYTES;
   const uint32_t s_ring = sbase + C::OFF_RING;
-  const uint32_t s_p0 = sbase + C::OFF_P, s_p1 = s_p0 + C::PBYTES;
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
   const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 16;
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(320, 1)
           ok = mbar_wait(b_p + 8 * t, j & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0), t ? s_p1 : s_p0,
+          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0), tmem + (t ? C::COL_S1 : C::COL_S0),
                       s_ring + slot_v * C::KVBYTES, j > 0);
           if (j + 1 < ntile[t]) {
             if (!have_k) {
@@ -273,7 +274,6 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
     const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
-    const uint32_t s_p = t ? s_p1 : s_p0;
     const int nt = ntile[t];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -331,18 +331,18 @@ __global__ void __launch_bounds__(320, 1)
       }
       const float moff = m_used;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        uint32_t w[4];
+      for (int c32 = 0; c32 < 4; ++c32) {   // P pairs over S columns 16*c32 ..
+        uint32_t w[16];
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float e0 = ex2(fmaf(s[8 * c8 + 2 * h], p.scale_log2, -moff));
-          const float e1 = ex2(fmaf(s[8 * c8 + 2 * h + 1], p.scale_log2, -moff));
+        for (int h = 0; h < 16; ++h) {
+          const float e0 = ex2(fmaf(s[32 * c32 + 2 * h], p.scale_log2, -moff));
+          const float e1 = ex2(fmaf(s[32 * c32 + 2 * h + 1], p.scale_log2, -moff));
           l += e0 + e1;
           w[h] = pack_half2(e0, e1);
         }
-        st_shared_v4(s_p + sw128_offset(r, c8, 128), w[0], w[1], w[2], w[3]);
+        tmem_st16(t_s + 16 * c32, w);
       }
-      fence_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p + 8 * t);
     }
