@@ -20,12 +20,14 @@
 // over the GQA group and all query blocks, keeping both accumulators in TMEM
 // (as the reference keeps them in registers, flash_bwd.cuh:163, :448-463).
 //
-// Workspace (written by the preprocess, read by both gradient kernels): per
-// (batch, q-head) a row of n_pad = roundup(N, 128) floats of Dv * scale, then
-// the same for LSE * log2(e). Padded rows hold 0 and +inf, so P = 0 there
+// Workspace (written by the preprocess, read by the gradient kernels): per
+// (batch, q-head) a row of n_pad = roundup(N, 128) floats of -Dv * scale, then
+// the same for -LSE * log2(e). Padded rows hold 0 and -inf, so P = 0 there
 // without a bounds test, and every 128-row slice starts 512-byte aligned, which
-// lets the TMA warp bulk-copy a query block's slice next to its Q tile. With
-// Dv pre-scaled, dS = scale * P o (dP - Dv) is P * fma(dP, scale, -Dv*scale).
+// lets the TMA warp bulk-copy a query block's slice next to its Q tile. Stored
+// negated and pre-scaled, P = 2^fma(S, scale*log2e, -LSE*log2e) and
+// dS = scale * P o (dP - Dv) = P * fma(dP, scale, -Dv*scale) are one FMA each,
+// which also runs on pairs of columns as one packed fp32x2 instruction.
 #pragma once
 #include "sm100.cuh"
 
@@ -35,8 +37,8 @@ struct BwdParams {
   const __half* o;     // (B*Hq, N, D) forward output
   const __half* dO;    // (B*Hq, N, D)
   const float* lse;    // (B*Hq, N) natural log
-  float* dvec;         // (B*Hq, n_pad) workspace: rowsum(dO o O) * scale
-  float* lse2;         // (B*Hq, n_pad) workspace: LSE * log2(e)
+  float* dvec;         // (B*Hq, n_pad) workspace: -rowsum(dO o O) * scale
+  float* lse2;         // (B*Hq, n_pad) workspace: -LSE * log2(e)
   void* dq;            // (B*Hq, N, D) fp32 or fp16
   __half* dk;          // (B*Hkv, N, D)
   __half* dv;          // (B*Hkv, N, D)
@@ -50,7 +52,7 @@ struct BwdParams {
 __host__ __device__ constexpr int pad_rows(int n) { return (n + 127) / 128 * 128; }
 
 // ---------------------------------------------------------------------------
-// Dv * scale = rowsum(dO o O) * scale and LSE * log2(e), over padded rows:
+// -Dv * scale = -rowsum(dO o O) * scale and -LSE * log2(e), over padded rows:
 // HBM-bound, one 16-byte vector per thread, D/8 threads per row reduced with
 // shuffles.
 // ---------------------------------------------------------------------------
@@ -93,8 +95,8 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
 #pragma unroll
   for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (prow < rows_pad && part == 0) {
-    dvec[prow] = real ? acc * scale : 0.f;
-    lse2[prow] = real ? __ldg(lse + row) * 1.4426950408889634f : INFINITY;
+    dvec[prow] = real ? -acc * scale : 0.f;
+    lse2[prow] = real ? __ldg(lse + row) * -1.4426950408889634f : -INFINITY;
   }
 }
 
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4) {
             const int c = 4 * c4 + e4;
-            pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lv[e4]));
+            pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, lv[e4]));
           }
         }
       // Masking is a separate pass, taken only by the steps that need it (the
@@ -482,7 +484,7 @@ __global__ void __launch_bounds__(320, 1)
           const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4)
-            pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, -dv[e4]);
+            pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, dv[e4]);
         }
       tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
       tmem_st_wait();
@@ -739,10 +741,10 @@ __global__ void __launch_bounds__(320, 1)
     const int r = threadIdx.x & 127;
     const int row = m0 + r;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    // padded rows (row >= N) read LSE = +inf, Dv = 0: their P and dS are 0
+    // padded rows (row >= N) read -LSE*log2e = -inf, Dv = 0: their P and dS are 0
     const size_t prow = static_cast<size_t>(bh) * p.n_pad + row;
-    const float lse2 = p.lse2[prow];
-    const float dvs = p.dvec[prow];   // Dv * scale
+    const float nlse2 = p.lse2[prow];   // -LSE * log2(e)
+    const float ndvs = p.dvec[prow];    // -Dv * scale
     const int klim = p.causal ? min(p.n - 1, row) : (p.n - 1);  // key live iff key <= klim
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -768,7 +770,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c)
-          pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lse2));
+          pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, nlse2));
       if (need_mask) {  // only the diagonal block and the ragged tail
 #pragma unroll
         for (int h = 0; h < 2; ++h)
@@ -794,7 +796,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pv[h][c] *= fmaf(__uint_as_float(sr[h][c]), p.scale, -dvs);
+        for (int c = 0; c < 32; ++c) pv[h][c] *= fmaf(__uint_as_float(sr[h][c]), p.scale, ndvs);
       tmem_st_pairs(tmem + C::COL_DS + 64 * (j & 1) + 32 * w + lane_off, pv);
       tmem_st_wait();
       tc_fence_before();
@@ -852,14 +854,16 @@ namespace fab {
 //   warp  8    TMEM allocation + MMA issue
 //   warp  9    TMA producer: K, V once; then Q_i (+ LSE/Dv slices), dO_i
 // TMEM: S^T 0..127, with P^T (fp16 pairs) written back over cols 32..95 |
-//       dP^T 128..255, then dQ_i once dS_i has been formed | dV 256.. | dK 256+D..
-// Shared: K, V, a 3-slot Q/dO ring, the dS^T tile [key][query], eight 4 KiB
+//       dP^T 128..255, with dS^T (fp16 pairs) written back over cols 160..223,
+//       then dQ_i | dV 256.. | dK 256+D..
+// Shared: K, V, a 3-slot Q/dO ring, the dS tile [key][query], eight 4 KiB
 // dQ staging boxes (one per compute warp; with D = 128 a warp's second box is
 // staged in its own rows of the dS tile), LSE/Dv slices for two steps.
 // MMA order per step i (brackets = what it waits for):
 //   [P_i] dV_i = P^T dO (A in TMEM) ; [Q_{i+1}] S^T_{i+1} ;
-//   [dS_i] dK_i = dS^T Q (A = the dS tile K-major), dQ_i = dS K (A = the same
-//   tile MN-major, into the dP^T columns) ; [dQ_i read, dO_{i+1}] dP^T_{i+1}
+//   [dS_i] dK_i = dS^T Q (A in TMEM), dQ_i = dS K (A = the dS tile read
+//   MN-major, into the dP^T columns, after dK_i has read dS^T there) ;
+//   [dQ_i read, dO_{i+1}] dP^T_{i+1}
 // and the compute warps run dS_i, P_{i+1}, dQ_i read-out, so that the P phase
 // of the next step overlaps dK_i and dQ_i on the tensor core.
 // Overwrites follow issue order (S^T_{i+1} after dV_i read P_i; dQ_i after
@@ -890,7 +894,7 @@ struct FusedCfg {
   static constexpr int NCOMPUTE = 256;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
-  static constexpr uint32_t COL_P = 32, COL_DQ = 128;
+  static constexpr uint32_t COL_P = 32, COL_DS = 160, COL_DQ = 128;
 };
 
 template <int D>
@@ -1009,7 +1013,7 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
       constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (TS), dK (SS)
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV, dK (TS)
       constexpr uint32_t id_q = idesc_f16(128, D, true, true);      // dQ: A = dS MN-major
       // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
@@ -1021,7 +1025,6 @@ __global__ void __launch_bounds__(320, 1)
         }
       };
       auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
-      const uint64_t d_dsk = sdesc_sw128(s_ds, 16, 1024);       // dS^T tile as K-major A
       const uint64_t d_dsm = sdesc_sw128(s_ds, 16384, 1024);    // dS tile as MN-major A
       const uint64_t d_kmn = sdesc_sw128(s_k, 16384, 1024);     // K as MN-major B
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
@@ -1068,8 +1071,8 @@ __global__ void __launch_bounds__(320, 1)
           const uint64_t dq_mn = sdesc_sw128(slot_addr(it_q), 16384, 1024);
 #pragma unroll
           for (int kk = 0; kk < C::BM / 16; ++kk)
-            mma_ss(tmem + C::COL_DK, sdesc_add(d_dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
-                   sdesc_add(dq_mn, kk * 2048), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tmem + C::COL_DK, tmem + C::COL_DS + kk * 8, sdesc_add(dq_mn, kk * 2048), id_g,
+                   (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(b_empty + 8 * slot_of(it_q));
 #pragma unroll
@@ -1121,16 +1124,20 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
       const float4* lse4 =
           reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4;
+      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 l4 = lse4[8 * h + c4];
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float4 l4 = lse4[8 * h + c4];   // -LSE*log2e of 4 query columns
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const int c = 4 * c4 + e4;
-            pv[h][c] = ex2(fmaf(__uint_as_float(sr[h][c]), p.scale_log2, -lv[e4]));
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int c = 4 * c4 + 2 * e2;
+            const float2 x = f32x2_split(
+                fma_x2(f32x2(__uint_as_float(sr[h][c]), __uint_as_float(sr[h][c + 1])), sl2,
+                       e2 ? f32x2(l4.z, l4.w) : f32x2(l4.x, l4.y)));
+            pv[h][c] = ex2(x.x);
+            pv[h][c + 1] = ex2(x.y);
           }
         }
       if (need_mask) {
@@ -1149,7 +1156,8 @@ __global__ void __launch_bounds__(320, 1)
       return true;
     };
 
-    // dS_i^T = P^T o (dP^T * scale - Dv*scale), into the shared [key][query] tile
+    // dS_i^T = P^T o (dP^T * scale - Dv*scale), into TMEM (for dK) and the
+    // shared [key][query] tile (for dQ)
     auto phase_ds = [&](int i) -> bool {
       bool ok = mbar_wait(b_dp, i & 1, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
@@ -1164,16 +1172,24 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
       const float4* dvs4 =
           reinterpret_cast<const float4*>(smem_raw + C::OFF_LSE) + ((i & 1) * 128 + 64 * w) / 4 + 64;
+      const uint64_t sc2 = f32x2(p.scale, p.scale);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 d4 = dvs4[8 * h + c4];
-          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+          const float4 d4 = dvs4[8 * h + c4];   // -Dv*scale of 4 query columns
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4)
-            pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, -dv[e4]);
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int c = 4 * c4 + 2 * e2;
+            const uint64_t t = fma_x2(f32x2(__uint_as_float(sr[h][c]), __uint_as_float(sr[h][c + 1])),
+                                      sc2, e2 ? f32x2(d4.z, d4.w) : f32x2(d4.x, d4.y));
+            const float2 ds = f32x2_split(mul_x2(f32x2(pv[h][c], pv[h][c + 1]), t));
+            pv[h][c] = ds.x;
+            pv[h][c + 1] = ds.y;
+          }
         }
+      // dS^T as fp16 pairs over dP^T columns this group has read (A of dK)
+      tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
       if constexpr (D / 64 > 1) {   // this warp's rows of the tile staged a dQ box
         if (lane == 0) bulk_wait_read_all_but_last();   // committed before box 0
         __syncwarp();
@@ -1181,6 +1197,7 @@ __global__ void __launch_bounds__(320, 1)
       st_row32_sw128(s_ds + w * 16384, r, 0, pv[0]);
       st_row32_sw128(s_ds + w * 16384, r, 1, pv[1]);
       fence_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_ds);
       return true;

@@ -299,9 +299,16 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 128; ++c)
           if (col0 + c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // row max: 8 interleaved chains of three-input maxima, then a tree
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+      for (int c = 0; c < 8; ++c) mx8[c] = s[c];
+#pragma unroll
+      for (int c = 8; c < 128; c += 16)
+#pragma unroll
+        for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
+      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
+                             max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       if (j == 0) {
         m_used = m_new;
@@ -329,19 +336,25 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st_wait();
         }
       }
-      const float moff = m_used;
+      // P = 2^(s*scale*log2e - m) on column pairs: one packed FMA and one
+      // packed add (row sum, two chains of pairs) per two columns
+      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
+      uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
 #pragma unroll
       for (int c32 = 0; c32 < 4; ++c32) {   // P pairs over S columns 16*c32 ..
         uint32_t w[16];
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
-          const float e0 = ex2(fmaf(s[32 * c32 + 2 * h], p.scale_log2, -moff));
-          const float e1 = ex2(fmaf(s[32 * c32 + 2 * h + 1], p.scale_log2, -moff));
-          l += e0 + e1;
+          const float2 x =
+              f32x2_split(fma_x2(f32x2(s[32 * c32 + 2 * h], s[32 * c32 + 2 * h + 1]), sl2, nm));
+          const float e0 = ex2(x.x), e1 = ex2(x.y);
+          lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
           w[h] = pack_half2(e0, e1);
         }
         tmem_st16(t_s + 16 * c32, w);
       }
+      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
+      l += la.x + la.y;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p + 8 * t);
