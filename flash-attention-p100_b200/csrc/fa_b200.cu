@@ -10,6 +10,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdarg>
@@ -253,7 +254,15 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     CUtensorMap tdq;
     if (!make_map(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, BH, 32))
       return FA_B200_ERR_TENSOR_MAP;
-    bwd_fused_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), FusedCfg<D>::THREADS,
+    // slices per scheduling group: a (batch, kv-head) slice's fp32 dQ rows and
+    // Q/dO tiles take group * N * D * 8 bytes; a group holds at most 64 MiB of
+    // them (half of L2), and the groups are made equal in size
+    const uint64_t slice_bytes = std::max<uint64_t>(static_cast<uint64_t>(p.group) * N * D * 8, 1);
+    const uint64_t hg_max = std::max<uint64_t>(1, (64ull << 20) / slice_bytes);
+    const uint64_t n_groups = (BHkv + hg_max - 1) / hg_max;
+    p.head_group = static_cast<int>((BHkv + n_groups - 1) / n_groups);
+    if (BHkv * static_cast<uint64_t>(nq128) > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
+    bwd_fused_kernel<D><<<static_cast<unsigned>(BHkv * nq128), FusedCfg<D>::THREADS,
                           FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
     if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
   }

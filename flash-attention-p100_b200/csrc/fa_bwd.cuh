@@ -45,6 +45,7 @@ struct BwdParams {
   int* err;
   int n, n_pad, hq, group, causal;
   int dq_fp32;
+  int head_group;      // fused kernel: (batch, kv-head) slices scheduled together
   float scale;         // 1/sqrt(D)
   float scale_log2;    // scale * log2(e)
 };
@@ -916,12 +917,24 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (B*Hkv, key blocks): causal key block 0 has the most work and goes
-  // first. CTAs that run together start at neighbouring query blocks and
-  // advance in step, so the Q/dO tiles and dQ rows they share stay in L2.
-  const int bkv = blockIdx.x;
-  const int kvb = blockIdx.y;
+  // 1-D grid over (batch, kv-head) slices x key blocks, scheduled in groups of
+  // p.head_group slices whose dQ rows and Q/dO tiles fit in L2 together; inside
+  // a group the causal key block 0 of every slice (the most work) goes first,
+  // then block 1, and so on. CTAs that run together start at neighbouring query
+  // blocks of the group's slices and advance in step, so the tiles they share
+  // and the dQ rows they add into are L2 hits rather than DRAM round trips.
+  const int nkb = (p.n + C::BN - 1) / C::BN;
   const int hkv = p.hq / p.group;
+  int bkv, kvb;
+  {
+    const int per_group = p.head_group * nkb;
+    const int g0 = static_cast<int>(blockIdx.x) / per_group;
+    const int r = static_cast<int>(blockIdx.x) - g0 * per_group;
+    const int n_bkv = (gridDim.x / nkb);                 // B * Hkv
+    const int hg = min(p.head_group, n_bkv - g0 * p.head_group);
+    kvb = r / hg;
+    bkv = g0 * p.head_group + r % hg;
+  }
   const int b = bkv / hkv, kvh = bkv % hkv;
   const int kv0 = kvb * C::BN;
   const int nqb = (p.n + C::BM - 1) / C::BM;
