@@ -51,16 +51,18 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum
  * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the
- * log2-scaled LSE, each head padded to roundup(N, 128) rows:
- * 2 * 4 * B * Hq * roundup(N, 128) bytes. */
+ * log2-scaled LSE (both stored negated and pre-scaled), each head padded to
+ * roundup(N, 128) rows: 2 * 4 * B * Hq * roundup(N, 128) bytes. */
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
 
 /* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
- * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq (fp32 when dq_fp32 != 0,
- * as the reference returns it, else fp16), dk and dv (fp16). dQ comes from its
- * own kernel that owns each dQ row (the reference adds it with fp32 atomics,
- * flash_bwd.cuh:442): no atomics, bitwise deterministic. The atomic variant is
- * available as FA_B200_STAGE_FUSED (see fa_b200_backward_stages). */
+ * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq, dk and dv (fp16).
+ * dq_fp32 != 0 (dq fp32, as the reference returns it): stages ROWSUM | FUSED --
+ * one kernel for dK, dV and dQ, dQ added into the zeroed fp32 dq by TMA
+ * reduce-adds, so like the reference's atomicAdd (flash_bwd.cuh:442) the last
+ * bits of dq depend on the add order. dq_fp32 == 0 (dq fp16): stages ALL --
+ * separate dK/dV and dQ kernels, each output row owned by one CTA, bitwise
+ * deterministic. */
 int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
                      const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
@@ -73,18 +75,19 @@ enum {
   FA_B200_STAGE_DKDV = 2,    /* dK, dV (reads the workspace) */
   FA_B200_STAGE_DQ = 4,      /* dQ (reads the workspace) */
   FA_B200_STAGE_ALL = 7,      /* ROWSUM | DKDV | DQ: the deterministic set */
-  FA_B200_STAGE_FUSED = 8     /* dK, dV and dQ in one kernel, dQ added with fp32 atomics
-                               * into a zeroed fp32 dq (the reference's scheme); needs
-                               * dq_fp32 and a prior ROWSUM stage (which zeroes dq);
-                               * excludes DKDV and DQ. Not bitwise deterministic, and on
-                               * B200 slower than DKDV + DQ: the atomics dominate */
+  FA_B200_STAGE_FUSED = 8     /* dK, dV and dQ in one kernel, dQ added by TMA reduce-adds
+                               * into a zeroed fp32 dq (the reference's accumulate-into-
+                               * fp32 scheme); needs dq_fp32 and a prior ROWSUM stage
+                               * (which zeroes dq); excludes DKDV and DQ. Not bitwise
+                               * deterministic; the default for dq_fp32 != 0 */
 };
 
 /* fa_b200_backward restricted to the stages in `stages`. The dK/dV and dQ
  * stages only read the row sums, so once FA_B200_STAGE_ROWSUM has run they may
  * be enqueued on two streams and overlap. fa_b200_backward(...) is
- * fa_b200_backward_stages(..., FA_B200_STAGE_ALL, stream). No counterpart in
- * the reference, whose backward is one launcher (flash_bwd.cuh:466-484). */
+ * fa_b200_backward_stages(..., ROWSUM | FUSED or ALL as described there,
+ * stream). No counterpart in the reference, whose backward is one launcher
+ * (flash_bwd.cuh:466-484). */
 int fa_b200_backward_stages(const void* q, const void* k, const void* v, const void* dO,
                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
