@@ -144,6 +144,15 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// FA_B200_OK, or FA_B200_ERR_LAUNCH with the CUDA error of the launch just made
+// (and its kernel's name) as the thread's last-error detail.
+int launch_status(const char* kernel) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return FA_B200_OK;
+  set_last_error("launch of %s failed: %s", kernel, cudaGetErrorString(e));
+  return FA_B200_ERR_LAUNCH;
+}
+
 // An fp32 dQ is produced by the fused kernel: one pass, dQ added into the
 // zeroed output by TMA reduce-adds (the reference's fp32 dQ contract, and like
 // its atomicAdd not bitwise deterministic). An fp16 dQ has no fp32 buffer to
@@ -198,7 +207,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
   if (p.n_mblocks > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
   dim3 grid(static_cast<unsigned>(BH), p.n_mblocks);
   fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? FA_B200_OK : FA_B200_ERR_LAUNCH;
+  return launch_status("fwd_kernel");
 }
 
 template <int D>
@@ -242,12 +251,12 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
         static_cast<const __half*>(o), static_cast<const __half*>(dO), lse, p.dvec, p.lse2, N,
         n_pad, rows_pad, p.scale,
         p.dq_fp32 ? static_cast<float*>(dq) : nullptr);
-    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+    if (int st = launch_status("bwd_preprocess_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DKDV) {
     bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
                          DkdvCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
-    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+    if (int st = launch_status("bwd_dkdv_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_FUSED) {
     // dQ (fp32) as 32-row x 32-column boxes for the TMA reduce-adds
@@ -264,12 +273,12 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     if (BHkv * static_cast<uint64_t>(nq128) > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
     bwd_fused_kernel<D><<<static_cast<unsigned>(BHkv * nq128), FusedCfg<D>::THREADS,
                           FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
-    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+    if (int st = launch_status("bwd_fused_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DQ) {
     bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
                        stream>>>(tq, tk, tv, tdo, p);
-    if (cudaGetLastError() != cudaSuccess) return FA_B200_ERR_LAUNCH;
+    if (int st = launch_status("bwd_dq_kernel")) return st;
   }
   return FA_B200_OK;
 }

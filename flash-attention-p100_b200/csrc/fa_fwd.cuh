@@ -9,15 +9,19 @@
 //
 // Structure of one CTA (persistent over nothing: one CTA = 256 query rows of
 // one (batch, q-head)):
-//   warps 0-3  softmax for query tile 0 (rows m0 .. m0+127), one thread per row
-//   warps 4-7  softmax for query tile 1 (rows m0+128 .. m0+255)
-//   warp  8    TMEM allocation + the single thread that issues tcgen05.mma
-//   warp  9    the single thread that issues TMA loads
+//   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): two warpgroups,
+//               thread r of group h takes row r, columns 64h .. 64h+63
+//   warps 8-15  softmax for query tile 1 (rows m0+128 .. m0+255), the same way
+//   warp  16    TMEM allocation + the single thread that issues tcgen05.mma
+//   warp  17    the single thread that issues TMA loads
+// Two warps per SMSP share one tile's exponentials; the two halves of a row
+// exchange their partial maxima (and, at the end, row sums) through shared
+// memory under a per-tile mbarrier.
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
-// P_t (fp16 pairs, column c = keys 2c, 2c+1) is written back over the first 64
-// columns of S_t: each softmax thread owns its row's TMEM lane and has the
-// whole S row in registers by then. O_t += P_t V_j reads P_t from TMEM, so
-// P never touches shared memory, and V is the MMA's only shared operand.
+// P_t (fp16 pairs, column 32 + c = keys 2c, 2c+1) is written back over
+// columns 32..95 of S_t: each half writes its 32 pair columns inside the 64 S
+// columns it has already read into registers. O_t += P_t V_j reads P_t from
+// TMEM, so P never touches shared memory, and V is the MMA's only shared operand.
 // Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate).
 //
 // Per key block j the MMA thread issues, in order,
@@ -52,17 +56,20 @@ struct FwdCfg {
   static constexpr int CH = D / 64;             // 64-column chunks per row
   static constexpr int QBYTES = BM * D * 2;
   static constexpr int KVBYTES = BN * D * 2;
-  static constexpr int STAGES = (D == 128) ? 5 : 8;
+  static constexpr int STAGES = (D == 128) ? 4 : 8;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
-  static constexpr int OFF_BAR = OFF_RING + STAGES * KVBYTES;
-  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin; then tmem addr + abort flag
-  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  static constexpr int OFF_X = OFF_RING + STAGES * KVBYTES;   // [tile][parity][half][row] floats
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 2 * 128 * 4;
+  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin, x[2]; then tmem addr + abort flag
+  static constexpr int NBAR = 1 + 2 * STAGES + 9;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 576;
+  static constexpr int MMA_WARP = 16, TMA_WARP = 17;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O0 = 256, COL_O1 = 256 + D;
+  static constexpr uint32_t COL_P = 32;   // P pairs inside S: columns 32..95
 };
 
 }  // namespace fab
@@ -96,7 +103,7 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __maxnreg__(96)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   using C = FwdCfg<D>;
@@ -109,7 +116,8 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
   const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 16;
-  const uint32_t b_fin = b_o + 16;
+  const uint32_t b_fin = b_o + 16, b_x = b_fin + 8;
+  float* xbuf = reinterpret_cast<float*>(sgen + C::OFF_X);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -137,20 +145,21 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(b_s + 8 * t, 1);
-      mbar_init(b_p + 8 * t, 128);
+      mbar_init(b_p + 8 * t, 256);
+      mbar_init(b_x + 8 * t, 256);
       mbar_init(b_o + 8 * t, 1);
     }
     mbar_init(b_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  if (warp == C::MMA_WARP) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == C::TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -197,7 +206,7 @@ __global__ void __launch_bounds__(320, 1)
         drain_loads(b_full, it, C::STAGES);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(b_q, 0, ctl, kErrTimeoutMma);
@@ -234,8 +243,9 @@ __global__ void __launch_bounds__(320, 1)
           ok = mbar_wait(b_p + 8 * t, j & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0), tmem + (t ? C::COL_S1 : C::COL_S0),
-                      s_ring + slot_v * C::KVBYTES, j > 0);
+          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0),
+                      tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P, s_ring + slot_v * C::KVBYTES,
+                      j > 0);
           if (j + 1 < ntile[t]) {
             if (!have_k) {
               ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
@@ -267,14 +277,19 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax tile t
-    const int t = warp >> 2;
+    // ------------------------------------------------------------ softmax tile t, half hf
+    const int t = warp >> 3;
+    const int hf = (warp >> 2) & 1;
     const int r = threadIdx.x & 127;
     const int row = m0 + 128 * t + r;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
     const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
+    const uint32_t bx = b_x + 8 * t;
+    // partial row values of this tile: xbuf[((t * 2 + parity) * 2 + half) * 128 + r]
+    auto xslot = [&](int par, int half) { return xbuf + ((t * 2 + par) * 2 + half) * 128 + r; };
     const int nt = ntile[t];
+    const int c0 = 64 * hf;                  // this half's first column of S
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -282,66 +297,66 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, sr[c]);
+      uint32_t sr[2][32];
+      tmem_ld32(t_s + c0, sr[0]);
+      tmem_ld32(t_s + c0 + 32, sr[1]);
       tmem_ld_wait_only();
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
       float* s = reinterpret_cast<float*>(&sr[0][0]);
-      const int col0 = j * 128;
-      const bool need_mask = (col0 + 128 > p.n) || (p.causal && col0 + 127 > m0 + 128 * t);
+      const int col0 = j * 128 + c0;
+      const bool need_mask = (j * 128 + 128 > p.n) || (p.causal && j * 128 + 127 > m0 + 128 * t);
       if (need_mask) {
         const int lim = p.causal ? min(p.n - 1, row) : (p.n - 1);
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
+        for (int c = 0; c < 64; ++c)
           if (col0 + c > lim) s[c] = -INFINITY;
       }
-      // row max: 8 interleaved chains of three-input maxima, then a tree
+      // this half's max: 8 interleaved chains of three-input maxima, then a tree
       float mx8[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx8[c] = s[c];
 #pragma unroll
-      for (int c = 8; c < 128; c += 16)
+      for (int c = 8; c < 64; c += 16)
 #pragma unroll
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
-      const float mx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
-                             max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
+      const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
+                              max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
+      // exchange with the other half of the row (buffer by step parity)
+      *xslot(j & 1, hf) = pmx;
+      mbar_arrive(bx);
+      ok = mbar_wait(bx, j & 1, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const float mx = fmaxf(pmx, *xslot(j & 1, hf ^ 1));
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
+      // Rescale only when the running max grew by more than 2^8: P stays
+      // below 256, and the final 1/l uses the same offset, so the result is
+      // unchanged (only which power of two the partial sums carry). Both
+      // halves see the same maxima and so take the same decision. O itself is
+      // rescaled after the exponentials (below), when S is no longer live.
+      bool rescale = false;
+      float alpha = 1.f;
       if (j == 0) {
         m_used = m_new;
       } else {
-        // Rescale only when the running max grew by more than 2^8: P stays
-        // below 256, and the final 1/l uses the same offset, so the result is
-        // unchanged (only which power of two the partial sums carry).
         const bool need = m_new > m_used + 8.f;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2(m_used - m_new) : 1.f;
-          if (need) {
-            l *= alpha;
-            m_used = m_new;
-          }
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t orow[32];
-            tmem_ld32(t_o + 32 * c, orow);
-            tmem_ld_wait(orow);
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            tmem_st32(t_o + 32 * c, orow);
-          }
-          tmem_st_wait();
+        rescale = __any_sync(0xffffffffu, need);
+        if (need) {
+          alpha = ex2(m_used - m_new);
+          l *= alpha;
+          m_used = m_new;
         }
       }
       // P = 2^(s*scale*log2e - m) on column pairs: one packed FMA and one
-      // packed add (row sum, two chains of pairs) per two columns
+      // packed add (row sum, two chains of pairs) per two columns; this half's
+      // 32 pair columns go to COL_P + 32*hf .., inside the S columns it read
       const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
       uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
 #pragma unroll
-      for (int c32 = 0; c32 < 4; ++c32) {   // P pairs over S columns 16*c32 ..
+      for (int c32 = 0; c32 < 2; ++c32) {
         uint32_t w[16];
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
@@ -351,26 +366,43 @@ __global__ void __launch_bounds__(320, 1)
           lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
           w[h] = pack_half2(e0, e1);
         }
-        tmem_st16(t_s + 16 * c32, w);
+        tmem_st16(t_s + C::COL_P + 32 * hf + 16 * c32, w);
       }
       const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
       l += la.x + la.y;
+      if (rescale) {   // O_t *= alpha on this half's D/2 columns, before P_t is released
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t orow[32];
+          const uint32_t a = t_o + hf * (D / 2) + 32 * c;
+          tmem_ld32(a, orow);
+          tmem_ld_wait(orow);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+          tmem_st32(a, orow);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p + 8 * t);
     }
     if (ok && nt > 0) {
-      ok = mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
+      // the row sum is the two halves' sums: one more exchange (phase nt)
+      *xslot(nt & 1, hf) = l;
+      mbar_arrive(bx);
+      ok = mbar_wait(bx, nt & 1, ctl, kErrTimeoutSoftmax) &&
+           mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
+        l += *xslot(nt & 1, hf ^ 1);
         tc_fence_after();
         const float inv = 1.f / l;
         const size_t bhn = static_cast<size_t>(bh) * p.n;
-        __half* orow_g = p.o + (bhn + row) * D;
+        __half* orow_g = p.o + (bhn + row) * D + hf * (D / 2);
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t orow[32];
-          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld32(t_o + hf * (D / 2) + 32 * c, orow);
           tmem_ld_wait(orow);
           if (row < p.n) {
 #pragma unroll
@@ -384,7 +416,7 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
-        if (row < p.n) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
+        if (row < p.n && hf == 0) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
       }
     }
   }
@@ -392,7 +424,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) {
+  if (warp == C::MMA_WARP) {
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
