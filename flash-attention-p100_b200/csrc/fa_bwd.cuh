@@ -845,30 +845,38 @@ namespace fab {
 // step's dQ contribution dQ_i = dS_i K and adds it into a zeroed fp32 dQ, as
 // the reference does with atomicAdd (flash_bwd.cuh:378-444) -- but with no
 // recompute of S and dP in a second kernel, and the adds done by the TMA unit:
-// each warp stages its 32 query rows x 32 columns of dQ_i (a 4 KiB swizzled
-// box) in shared memory and issues one tiled reduce-add of the box into global
-// memory, so the adds are coalesced 128-byte rows and run asynchronously.
-// The add order varies from run to run, so dQ is not bitwise deterministic.
-//   warps 0-7  compute: two warpgroups; thread r is key row r for P and dS and
-//              query row r of dQ_i; group w owns queries (and dQ columns)
-//              64w.. of each step
-//   warp  8    TMEM allocation + MMA issue
-//   warp  9    TMA producer: K, V once; then Q_i (+ LSE/Dv slices), dO_i
+// a read-out warpgroup stages dQ_i as 32-row x 32-column fp32 boxes (4 KiB,
+// swizzled) in shared memory and issues one tiled reduce-add per box into
+// global memory, so the adds are coalesced 128-byte rows and run
+// asynchronously. The add order varies from run to run, so dQ is not bitwise
+// deterministic.
+//   warps 0-7   compute: two warpgroups; thread r is key row r for P and dS;
+//               group w owns queries 64w.. of each step
+//   warps 8-11  dQ read-out: warp 8+q reads TMEM lanes 32q.. (query rows) of
+//               dQ_i, frees the columns, then stages and adds its boxes
+//   warp  12    TMEM allocation + MMA issue
+//   warp  13    TMA producer: K, V once; then Q_i (+ LSE/Dv slices), dO_i
+//   warps 14-15 idle (they complete the last warpgroup)
+// Registers are launched at 128 a thread and rebalanced per warpgroup
+// (setmaxnreg): compute 160, read-out 144, the MMA/TMA warpgroup 48; per lane
+// of an SMSP 160 + 160 + 144 + 48 = 512 = the 4 x 128 launched.
 // TMEM: S^T 0..127, with P^T (fp16 pairs) written back over cols 32..95 |
 //       dP^T 128..255, with dS^T (fp16 pairs) written back over cols 160..223,
-//       then dQ_i | dV 256.. | dK 256+D..
-// Shared: K, V, a 3-slot Q/dO ring, the dS tile [key][query], eight 4 KiB
-// dQ staging boxes (one per compute warp; with D = 128 a warp's second box is
-// staged in its own rows of the dS tile), LSE/Dv slices for two steps.
+//       then (D = 128) dQ_i | dV 256.. | dK 256+D.. | (D = 64) dQ 384..
+// Shared: K, V, a 3-slot Q/dO ring, the dS tile [key][query], two 4 KiB dQ
+// staging boxes per read-out warp, LSE/Dv slices for two steps.
 // MMA order per step i (brackets = what it waits for):
 //   [P_i] dV_i = P^T dO (A in TMEM) ; [Q_{i+1}] S^T_{i+1} ;
 //   [dS_i] dK_i = dS^T Q (A in TMEM), dQ_i = dS K (A = the dS tile read
 //   MN-major, into the dP^T columns, after dK_i has read dS^T there) ;
-//   [dQ_i read, dO_{i+1}] dP^T_{i+1}
-// and the compute warps run dS_i, P_{i+1}, dQ_i read-out, so that the P phase
-// of the next step overlaps dK_i and dQ_i on the tensor core.
+//   [dQ_i read, dO_{i+1}] dP^T_{i+1}   (D = 128; with D = 64 dQ has columns
+//   of its own and the dQ_i read gates dQ_{i+1} instead)
+// and the compute warps run dS_i, then P_{i+1}, so that the P phase of the
+// next step overlaps dK_i and dQ_i on the tensor core; the read-out warps take
+// dQ_i off the tensor memory as soon as it is complete.
 // Overwrites follow issue order (S^T_{i+1} after dV_i read P_i; dQ_i after
-// the compute threads read dP_i; dP^T_{i+1} after they read dQ_i). The dS
+// the compute threads read dP_i; dP^T_{i+1} after the read-out warps read
+// dQ_i). The dS
 // tile is rewritten for step i+1 only after dP^T_{i+1} completed, which was
 // issued after dK_i and dQ_i. The Q slot of step i is released after dK_i and
 // the producer fills the ring in order, so the LSE/Dv slice buffer i & 1 is
@@ -884,22 +892,30 @@ struct FusedCfg {
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_RING = OFF_V + TILE;
   static constexpr int OFF_DS = OFF_RING + STAGES * TILE;    // 128 keys x 128 queries fp16
-  static constexpr int OFF_STG = OFF_DS + 32768;             // 8 x (32 rows x 32 fp32)
+  static constexpr int OFF_STG = OFF_DS + 32768;             // 4 warps x 2 x (32 rows x 32 fp32)
   static constexpr int OFF_LSE = OFF_STG + 8 * 4096;         // [2][128] LSE*log2e, [2][128] Dv*scale
   static constexpr int OFF_BAR = OFF_LSE + 2048;
   // kv, full[ST], empty[ST], s, dp, p, ds, dqfull, dqfree, fin
   static constexpr int NBAR = 1 + 2 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;     // window must start 1024-aligned
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
-  static constexpr int THREADS = 320;
-  static constexpr int NCOMPUTE = 256;
+  static constexpr int THREADS = 512;
+  static constexpr int NCOMPUTE = 256, NREADOUT = 128;
+  static constexpr int MMA_WARP = 12, TMA_WARP = 13;
+  static constexpr int REGS_COMPUTE = 144, REGS_READOUT = 152, REGS_CONTROL = 72;
+  static_assert(2 * REGS_COMPUTE + REGS_READOUT + REGS_CONTROL <= 4 * 128,
+                "warpgroup register budgets exceed the 128 per thread launched");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 256 + D;
-  static constexpr uint32_t COL_P = 32, COL_DS = 160, COL_DQ = 128;
+  // D = 128 fills TMEM, so dQ_i goes into the dP^T columns and dP^T_{i+1}
+  // waits for it to be read out; D = 64 leaves columns 384.. free for a dQ of
+  // its own, and only dQ_{i+1} waits for the read-out of dQ_i.
+  static constexpr bool DQ_OWN_COLS = (D == 64);
+  static constexpr uint32_t COL_P = 32, COL_DS = 160, COL_DQ = DQ_OWN_COLS ? 384 : 128;
 };
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(512, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
@@ -956,18 +972,21 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(b_p, C::NCOMPUTE);
     mbar_init(b_ds, C::NCOMPUTE);
     mbar_init(b_dqfull, 1);
-    mbar_init(b_dqfree, C::NCOMPUTE);
+    mbar_init(b_dqfree, C::NREADOUT);
     mbar_init(b_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  if (warp == C::MMA_WARP) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp >= C::MMA_WARP) {
+    regs_lower<C::REGS_CONTROL>();
+  }
+  if (warp == C::TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -1022,7 +1041,7 @@ __global__ void __launch_bounds__(320, 1)
         drain_loads(b_full, it, C::STAGES);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
       constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
@@ -1088,13 +1107,18 @@ __global__ void __launch_bounds__(320, 1)
                    (i > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(b_empty + 8 * slot_of(it_q));
+        if (C::DQ_OWN_COLS && i > 0) {   // dQ_{i-1} has been read out of its columns
+          ok = mbar_wait(b_dqfree, (i - 1) & 1, ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+        }
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk)
           mma_ss(tmem + C::COL_DQ, sdesc_add(d_dsm, kk * 2048), sdesc_add(d_kmn, kk * 2048), id_q,
                  kk > 0 ? 1u : 0u);
         mma_commit(b_dqfull);
         if (more) {
-          ok = mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma) &&
+          ok = (C::DQ_OWN_COLS || mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma)) &&
                mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
@@ -1107,14 +1131,65 @@ __global__ void __launch_bounds__(320, 1)
       while (!mbar_try_wait(b_fin, 0) && globaltimer_ns() - t0 < FAB_WAIT_LIMIT_NS) {
       }
     }
-  } else {
+  } else if (warp >= 8 && warp < 12) {
+    regs_raise<C::REGS_READOUT>();
+    // ------------------------------------------------------------ dQ read-out (warps 8-11)
+    // Warp 8+q takes TMEM lanes 32q.. (query rows qb0+32q..) of dQ_i, all D
+    // columns, frees the columns for dP^T_{i+1}, then stages its D/32 boxes of
+    // 32 x 32 fp32 through two alternating 4 KiB buffers and adds each into dQ
+    // with a TMA reduce-add. Boxes are committed one bulk group each, buffers
+    // alternate, and a warp with no rows below N stages nothing, so the group
+    // that last read a buffer is always the second most recent one.
+    const int q = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t stg = sbase + C::OFF_STG + (warp - 8) * 8192;
+    constexpr int NB = D / 32;
+    bool ok = true;
+    for (int i = 0; i < total && ok; ++i) {
+      const int qb0 = (i_start + i % nq_head) * C::BM;
+      const int bh = b * p.hq + kvh * p.group + i / nq_head;
+      ok = mbar_wait(b_dqfull, i & 1, ctl, kErrTimeoutEpilogue);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v[NB][32];
+#pragma unroll
+      for (int h = 0; h < NB; ++h) tmem_ld32(tmem + C::COL_DQ + 32 * h + lane_off, v[h]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int h = 0; h < NB; ++h)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(v[h][c]));
+      tc_fence_before();
+      mbar_arrive(b_dqfree);     // dP^T_{i+1} may overwrite the dQ_i columns
+      const int row0 = qb0 + 32 * q;
+      if (row0 >= p.n) continue;   // every row of this box is past N
+#pragma unroll
+      for (int h = 0; h < NB; ++h) {
+        const uint32_t box = stg + (h & 1) * 4096;
+        if (lane == 0) bulk_wait_read_all_but_last();   // this buffer's last box has been read
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(box + lane * 128 + ((c ^ (lane & 7)) << 4), v[h][4 * c], v[h][4 * c + 1],
+                       v[h][4 * c + 2], v[h][4 * c + 3]);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tm_dq, box, 32 * h, row0, bh);
+          bulk_commit_group();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();   // every dQ box added before the CTA exits
+  } else if (warp < 8) {
+    regs_raise<C::REGS_COMPUTE>();
     // ------------------------------------------------------------ compute (warps 0-7)
     const int w = warp >> 2;            // query half of each step
     const int r = threadIdx.x & 127;    // key row within the block
     const int kvrow = kv0 + r;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int qlim = p.causal ? kvrow : -1;  // a query column is live iff qlim <= q < N
-    const uint32_t stg = sbase + C::OFF_STG + warp * 4096;   // this warp's dQ box
     uint32_t sr[2][32];
     float pv[2][32];
 
@@ -1203,10 +1278,6 @@ __global__ void __launch_bounds__(320, 1)
         }
       // dS^T as fp16 pairs over dP^T columns this group has read (A of dK)
       tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
-      if constexpr (D / 64 > 1) {   // this warp's rows of the tile staged a dQ box
-        if (lane == 0) bulk_wait_read_all_but_last();   // committed before box 0
-        __syncwarp();
-      }
       st_row32_sw128(s_ds + w * 16384, r, 0, pv[0]);
       st_row32_sw128(s_ds + w * 16384, r, 1, pv[1]);
       fence_async_smem();
@@ -1216,64 +1287,12 @@ __global__ void __launch_bounds__(320, 1)
       return true;
     };
 
-    // dQ_i read-out: TMEM lane r is query row qb0 + r; group w takes dQ
-    // columns w*D/2 .. +D/2, in boxes of 32 rows x 32 columns, each staged in
-    // shared memory and added into global dQ by the TMA unit. Box 0 goes to
-    // this warp's staging buffer; box 1 (D = 128) to the warp's own 4 KiB of
-    // the dS tile -- its 32 rows of one query half, which dK_i and dQ_i have
-    // finished reading and which the warp rewrites only in its next dS phase,
-    // after waiting for the TMA to have read the box. Box 1 is issued and
-    // committed first, so that wait does not include box 0.
-    auto phase_ro = [&](int i) -> bool {
-      const int qb0 = (i_start + i % nq_head) * C::BM;
-      const int bh = b * p.hq + kvh * p.group + i / nq_head;
-      bool ok = mbar_wait(b_dqfull, i & 1, ctl, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) return false;
-      tc_fence_after();
-      constexpr int NB = D / 64;   // 32-column boxes per group
-#pragma unroll
-      for (int h = 0; h < NB; ++h)
-        tmem_ld32(tmem + C::COL_DQ + w * (D / 2) + 32 * h + lane_off, sr[h]);
-      tmem_ld_wait_only();
-#pragma unroll
-      for (int h = 0; h < NB; ++h)
-#pragma unroll
-        for (int c = 0; c < 32; ++c) asm volatile("" : "+r"(sr[h][c]));
-      tc_fence_before();
-      mbar_arrive(b_dqfree);      // dP^T_{i+1} may overwrite the dQ_i columns
-      const int row0 = qb0 + 32 * (warp & 3);
-      if (lane == 0) bulk_wait_read_all();     // last step's box 0 has left the buffer
-      __syncwarp();
-#pragma unroll
-      for (int h = 0; h < NB; ++h) {
-        const uint32_t box = h == 0 ? stg : s_ds + w * 16384 + (warp & 3) * 4096;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          st_shared_v4(box + lane * 128 + ((c ^ (lane & 7)) << 4), sr[h][4 * c], sr[h][4 * c + 1],
-                       sr[h][4 * c + 2], sr[h][4 * c + 3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0 && row0 < p.n) {
-#pragma unroll
-        for (int h = NB - 1; h >= 0; --h) {
-          tma_reduce_add_3d(&tm_dq, h == 0 ? stg : s_ds + w * 16384 + (warp & 3) * 4096,
-                            w * (D / 2) + 32 * h, row0, bh);
-          bulk_commit_group();
-        }
-      }
-      return true;
-    };
-
     bool ok = true;
     if (total > 0) ok = phase_p(0);
     for (int i = 0; i < total && ok; ++i) {
       ok = phase_ds(i);
       if (ok && i + 1 < total) ok = phase_p(i + 1);
-      if (ok) ok = phase_ro(i);
     }
-    if (lane == 0) bulk_wait_all();   // every dQ box added before the CTA exits
     if (ok && total > 0) {
       ok = mbar_wait(b_fin, 0, ctl, kErrTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok);
@@ -1296,7 +1315,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) {
+  if (warp == C::MMA_WARP) {
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

@@ -336,6 +336,18 @@ __device__ __forceinline__ void tmem_st_wait() {
 }
 
 // ---------------------------------------------------------------------------
+// per-warpgroup register budgets (every warp of the warpgroup executes these)
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void regs_raise() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_lower() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ---------------------------------------------------------------------------
 // packed fp32 pairs (sm_100 issues one instruction for two IEEE fp32 lanes)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
