@@ -10,12 +10,26 @@ import os
 
 from _build import LIB_PATH, build, up_to_date
 
+
+
+class Strides(ctypes.Structure):
+    """fa_b200_strides: element strides (batch, head, row) of a (B, H, N, D)
+    tensor whose D axis is contiguous."""
+    _fields_ = [("batch", ctypes.c_int64), ("head", ctypes.c_int64), ("row", ctypes.c_int64)]
+
+
 # The symbols include/fa_b200.h declares, with their ctypes signatures.
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _SZ = ctypes.c_size_t
+_S = Strides
 SIGNATURES = {
     "fa_b200_forward": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "fa_b200_forward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P,
+                                     _I, _I, _I, _I, _I, _I, _I, _P]),
+    "fa_b200_backward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P,
+                                      _P, _S, _I, _P, _S, _P, _S, _P, _SZ,
+                                      _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_workspace_bytes": (_SZ, [_I, _I, _I]),
     "fa_b200_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                               _I, _I, _I, _I, _I, _I, _P]),
@@ -58,6 +72,22 @@ def check(code, what):
         detail = lib().fa_b200_last_error().decode()
         raise RuntimeError(f"{what}: {status_string(code)} (status {code})"
                            + (f": {detail}" if detail else ""))
+
+
+def strides_of(t):
+    """fa_b200_strides of a (B, H, N, D) tensor with a contiguous D axis; None
+    if the layout does not qualify (the caller then passes a contiguous copy).
+    A stride of a size-1 dimension is never used to address anything and is
+    replaced by the contiguous one, which always satisfies the 16-byte rule."""
+    if t.dim() != 4 or t.stride(3) != 1 or t.data_ptr() % 16:
+        return None
+    unit = 16 // t.element_size()
+    B, H, N, D = t.shape
+    dense = (H * N * D, N * D, D)
+    st = [dense[i] if t.size(i) == 1 else t.stride(i) for i in range(3)]
+    if any(x < 0 or x % unit for x in st):
+        return None
+    return Strides(*st)
 
 
 def device_error(device=0, reset=True):

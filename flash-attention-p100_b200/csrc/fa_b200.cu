@@ -142,7 +142,49 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem
   return r == CUDA_SUCCESS;
 }
 
+// 4-D view (D, N, H, B) of a (B, H, N, D) tensor with element strides `st`
+// (the D axis contiguous), 128-byte swizzled boxes of box_rows x 128 bytes of
+// columns. Rows past N read as zero; reduce-adds skip them.
+bool make_map4(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
+               uint64_t cols, uint64_t rows, uint64_t heads, uint64_t batch, const Strides& st,
+               uint32_t box_rows) {
+  const cuuint64_t dims[4] = {cols, rows, heads, batch};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st.n) * elem_bytes,
+                                 static_cast<cuuint64_t>(st.h) * elem_bytes,
+                                 static_cast<cuuint64_t>(st.b) * elem_bytes};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / elem_bytes), box_rows, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = g_encode(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_last_error(
+        "cuTensorMapEncodeTiled -> CUresult %d for base %p, dims {%llu, %llu, %llu, %llu}, "
+        "strides {%llu, %llu, %llu} bytes, box {%u, %u, 1, 1}",
+        static_cast<int>(r), base, static_cast<unsigned long long>(cols),
+        static_cast<unsigned long long>(rows), static_cast<unsigned long long>(heads),
+        static_cast<unsigned long long>(batch), static_cast<unsigned long long>(strides[0]),
+        static_cast<unsigned long long>(strides[1]), static_cast<unsigned long long>(strides[2]),
+        box[0], box[1]);
+  return r == CUDA_SUCCESS;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+Strides contiguous(int H, int N, int D) {
+  return Strides{static_cast<long long>(H) * N * D, static_cast<long long>(N) * D, D};
+}
+
+// Element strides a tensor map and 16-byte vector accesses can use: every
+// stride non-negative and a multiple of 16 bytes.
+bool strides_ok(const Strides& st, int elem_bytes) {
+  const long long unit = 16 / elem_bytes;
+  return st.b >= 0 && st.h >= 0 && st.n >= 0 && st.b % unit == 0 && st.h % unit == 0 &&
+         st.n % unit == 0;
+}
+
+struct FwdLayout { Strides q, k, v, o; };
+struct BwdLayout { Strides q, k, v, dO, o, dq, dk, dv; };
 
 // FA_B200_OK, or FA_B200_ERR_LAUNCH with the CUDA error of the launch just made
 // (and its kernel's name) as the thread's last-error detail.
@@ -186,16 +228,17 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
 
 template <int D>
 int launch_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                   int Hkv, int N, int causal, cudaStream_t stream, int* err) {
+                   int Hkv, int N, int causal, const FwdLayout& L, cudaStream_t stream, int* err) {
   using C = FwdCfg<D>;
   CUtensorMap tq, tk, tv;
-  const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
-  if (!make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
-      !make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
-      !make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128))
+  const uint64_t BH = static_cast<uint64_t>(B) * Hq;
+  if (!make_map4(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.q, 128) ||
+      !make_map4(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.k, 128) ||
+      !make_map4(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.v, 128))
     return FA_B200_ERR_TENSOR_MAP;
   FwdParams p;
   p.o = static_cast<__half*>(o);
+  p.so = L.o;
   p.lse = lse;
   p.err = err;
   p.n = N;
@@ -213,20 +256,26 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
 template <int D>
 int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
                     const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* ws, int B,
-                    int Hq, int Hkv, int N, int causal, int stages, cudaStream_t stream, int* err) {
+                    int Hq, int Hkv, int N, int causal, int stages, const BwdLayout& L,
+                    cudaStream_t stream, int* err) {
   const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
   const int nq128 = (N + 127) / 128;
   if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-  // Every operand tile of both gradient kernels is 128 rows.
+  // Every operand tile of the gradient kernels is 128 rows.
   CUtensorMap tq, tdo, tk, tv;
-  if (!make_map(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
-      !make_map(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BH, 128) ||
-      !make_map(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128) ||
-      !make_map(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, BHkv, 128))
+  if (!make_map4(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.q, 128) ||
+      !make_map4(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.dO, 128) ||
+      !make_map4(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.k, 128) ||
+      !make_map4(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.v, 128))
     return FA_B200_ERR_TENSOR_MAP;
   BwdParams p;
   p.o = static_cast<const __half*>(o);
   p.dO = static_cast<const __half*>(dO);
+  p.so = L.o;
+  p.sdo = L.dO;
+  p.sdq = L.dq;
+  p.sdk = L.dk;
+  p.sdv = L.dv;
   p.lse = lse;
   const int n_pad = pad_rows(N);
   const long long rows_pad = static_cast<long long>(BH) * n_pad;
@@ -248,9 +297,9 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   if (stages & FA_B200_STAGE_ROWSUM) {
     const long long threads = rows_pad * (D / 8);
     bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const __half*>(o), static_cast<const __half*>(dO), lse, p.dvec, p.lse2, N,
-        n_pad, rows_pad, p.scale,
-        p.dq_fp32 ? static_cast<float*>(dq) : nullptr);
+        static_cast<const __half*>(o), L.o, static_cast<const __half*>(dO), L.dO, lse, p.dvec,
+        p.lse2, N, n_pad, Hq, rows_pad, p.scale, p.dq_fp32 ? static_cast<float*>(dq) : nullptr,
+        L.dq);
     if (int st = launch_status("bwd_preprocess_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DKDV) {
@@ -261,7 +310,7 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   if (stages & FA_B200_STAGE_FUSED) {
     // dQ (fp32) as 32-row x 32-column boxes for the TMA reduce-adds
     CUtensorMap tdq;
-    if (!make_map(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, BH, 32))
+    if (!make_map4(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hq, B, L.dq, 32))
       return FA_B200_ERR_TENSOR_MAP;
     // slices per scheduling group: a (batch, kv-head) slice's fp32 dQ rows and
     // Q/dO tiles take group * N * D * 8 bytes; a group holds at most 64 MiB of
@@ -391,27 +440,104 @@ __global__ void __launch_bounds__(192, 1)
 
 }  // namespace fab
 
+// Shared implementation of the contiguous and strided entry points.
+namespace fab {
+namespace {
+
+Strides from_abi(fa_b200_strides st) { return Strides{st.batch, st.head, st.row}; }
+
+int forward_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
+                 int Hkv, int N, int D, int causal, const FwdLayout& L, void* stream) {
+  if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
+  int st = check_shape(B, Hq, Hkv, N, D);
+  if (st != FA_B200_OK) return st;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(lse) ||
+      !strides_ok(L.q, 2) || !strides_ok(L.k, 2) || !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
+    return FA_B200_ERR_ALIGNMENT;
+  int dev = 0;
+  int* err = nullptr;
+  st = device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  return D == 64 ? launch_forward<64>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
+                 : launch_forward<128>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
+}
+
+// ws == nullptr: the built-in scratch of fa_b200_backward_noalloc.
+int backward_impl(const void* q, const void* k, const void* v, const void* dO, const void* o,
+                  const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
+                  size_t workspace_bytes, bool noalloc, int B, int Hq, int Hkv, int N, int D,
+                  int causal, int stages, const BwdLayout& L, void* stream) {
+  if (stages == 0) stages = default_stages(dq_fp32);
+  if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
+  if ((stages & FA_B200_STAGE_FUSED) && (!dq_fp32 || (stages & (FA_B200_STAGE_DKDV | FA_B200_STAGE_DQ))))
+    return FA_B200_ERR_SHAPE;
+  if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
+  int st = check_shape(B, Hq, Hkv, N, D);
+  if (st != FA_B200_OK) return st;
+  if (noalloc) {
+    const size_t rows = static_cast<size_t>(B) * Hq * pad_rows(N);
+    if (rows > kNoAllocRows) {
+      set_last_error(
+          "fa_b200_backward_noalloc: B*Hq*roundup(N,128) = %zu query rows exceeds the built-in "
+          "scratch of %zu rows (16 MiB); call fa_b200_backward with a caller-allocated workspace "
+          "instead",
+          rows, kNoAllocRows);
+      return FA_B200_ERR_SCRATCH_LIMIT;
+    }
+  } else if (!workspace || workspace_bytes < fa_b200_backward_workspace_bytes(B, Hq, N)) {
+    return FA_B200_ERR_WORKSPACE;
+  }
+  const void* ptrs[] = {q, k, v, dO, o, lse, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
+  if ((!noalloc && !aligned16(workspace)) || !strides_ok(L.q, 2) || !strides_ok(L.k, 2) ||
+      !strides_ok(L.v, 2) || !strides_ok(L.dO, 2) || !strides_ok(L.o, 2) ||
+      !strides_ok(L.dq, dq_fp32 ? 4 : 2) || !strides_ok(L.dk, 2) || !strides_ok(L.dv, 2))
+    return FA_B200_ERR_ALIGNMENT;
+  int dev = 0;
+  int* err = nullptr;
+  st = device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  float* ws = noalloc ? noalloc_scratch(dev) : static_cast<float*>(workspace);
+  if (!ws) return FA_B200_ERR_DEVICE;
+  auto s = static_cast<cudaStream_t>(stream);
+  return D == 64 ? launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv, N,
+                                       causal, stages, L, s, err)
+                 : launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv,
+                                        N, causal, stages, L, s, err);
+}
+
+BwdLayout contiguous_bwd(int Hq, int Hkv, int N, int D) {
+  const Strides sq = contiguous(Hq, N, D), skv = contiguous(Hkv, N, D);
+  return BwdLayout{sq, skv, skv, sq, sq, sq, skv, skv};
+}
+
+}  // namespace
+}  // namespace fab
+
 // ===========================================================================
 // extern "C" entry points
-// ===========================================================================
 extern "C" {
+
 
 int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
                     int Hkv, int N, int D, int causal, int full_precision, void* stream) {
   (void)full_precision;
-  if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
-  int st = fab::check_shape(B, Hq, Hkv, N, D);
-  if (st != FA_B200_OK) return st;
-  if (!fab::aligned16(q) || !fab::aligned16(k) || !fab::aligned16(v) || !fab::aligned16(o) ||
-      !fab::aligned16(lse))
-    return FA_B200_ERR_ALIGNMENT;
-  int dev = 0;
-  int* err = nullptr;
-  st = fab::device_setup(&dev, &err);
-  if (st != FA_B200_OK) return st;
-  auto s = static_cast<cudaStream_t>(stream);
-  return D == 64 ? fab::launch_forward<64>(q, k, v, o, lse, B, Hq, Hkv, N, causal, s, err)
-                 : fab::launch_forward<128>(q, k, v, o, lse, B, Hq, Hkv, N, causal, s, err);
+  const fab::Strides sq = fab::contiguous(Hq, N, D), skv = fab::contiguous(Hkv, N, D);
+  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, causal,
+                           fab::FwdLayout{sq, skv, skv, sq}, stream);
+}
+
+int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
+                            const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
+                            float* lse, int B, int Hq, int Hkv, int N, int D, int causal,
+                            int full_precision, void* stream) {
+  (void)full_precision;
+  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, causal,
+                           fab::FwdLayout{fab::from_abi(sq), fab::from_abi(sk), fab::from_abi(sv),
+                                          fab::from_abi(so)},
+                           stream);
 }
 
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {
@@ -425,36 +551,35 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream) {
-  return fa_b200_backward_stages(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace,
-                                 workspace_bytes, B, Hq, Hkv, N, D, causal,
-                                 fab::default_stages(dq_fp32), stream);
+  return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
+                            false, B, Hq, Hkv, N, D, causal, 0,
+                            fab::contiguous_bwd(Hq, Hkv, N, D), stream);
 }
 
 int fa_b200_backward_stages(const void* q, const void* k, const void* v, const void* dO,
                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
                             int Hkv, int N, int D, int causal, int stages, void* stream) {
-  if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
-  if ((stages & FA_B200_STAGE_FUSED) && (!dq_fp32 || (stages & (FA_B200_STAGE_DKDV | FA_B200_STAGE_DQ))))
-    return FA_B200_ERR_SHAPE;
-  if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
-  int st = fab::check_shape(B, Hq, Hkv, N, D);
-  if (st != FA_B200_OK) return st;
-  if (!workspace || workspace_bytes < fa_b200_backward_workspace_bytes(B, Hq, N))
-    return FA_B200_ERR_WORKSPACE;
-  const void* ptrs[] = {q, k, v, dO, o, lse, dq, dk, dv, workspace};
-  for (const void* ptr : ptrs)
-    if (!fab::aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
-  int dev = 0;
-  int* err = nullptr;
-  st = fab::device_setup(&dev, &err);
-  if (st != FA_B200_OK) return st;
-  auto s = static_cast<cudaStream_t>(stream);
-  float* ws = static_cast<float*>(workspace);
-  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                            Hkv, N, causal, stages, s, err)
-                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                             Hkv, N, causal, stages, s, err);
+  if (stages == 0) return FA_B200_ERR_SHAPE;
+  return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
+                            false, B, Hq, Hkv, N, D, causal, stages,
+                            fab::contiguous_bwd(Hq, Hkv, N, D), stream);
+}
+
+int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
+                             const void* v, fa_b200_strides sv, const void* dO,
+                             fa_b200_strides sdo, const void* o, fa_b200_strides so,
+                             const float* lse, void* dq, fa_b200_strides sdq, int dq_fp32,
+                             void* dk, fa_b200_strides sdk, void* dv, fa_b200_strides sdv,
+                             void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
+                             int N, int D, int causal, int stages, void* stream) {
+  using fab::from_abi;
+  return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
+                            false, B, Hq, Hkv, N, D, causal, stages,
+                            fab::BwdLayout{from_abi(sq), from_abi(sk), from_abi(sv), from_abi(sdo),
+                                           from_abi(so), from_abi(sdq), from_abi(sdk),
+                                           from_abi(sdv)},
+                            stream);
 }
 
 size_t fa_b200_backward_noalloc_max_rows(void) { return fab::kNoAllocRows; }
@@ -463,33 +588,8 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
                              const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                              void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
                              void* stream) {
-  if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
-  int st = fab::check_shape(B, Hq, Hkv, N, D);
-  if (st != FA_B200_OK) return st;
-  const size_t rows = static_cast<size_t>(B) * Hq * fab::pad_rows(N);
-  if (rows > fab::kNoAllocRows) {
-    fab::set_last_error(
-        "fa_b200_backward_noalloc: B*Hq*roundup(N,128) = %zu query rows exceeds the built-in "
-        "scratch of %zu rows (16 MiB); call fa_b200_backward with a caller-allocated workspace "
-        "instead",
-        rows, fab::kNoAllocRows);
-    return FA_B200_ERR_SCRATCH_LIMIT;
-  }
-  const void* ptrs[] = {q, k, v, dO, o, lse, dq, dk, dv};
-  for (const void* ptr : ptrs)
-    if (!fab::aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
-  int dev = 0;
-  int* err = nullptr;
-  st = fab::device_setup(&dev, &err);
-  if (st != FA_B200_OK) return st;
-  float* ws = fab::noalloc_scratch(dev);
-  if (!ws) return FA_B200_ERR_DEVICE;
-  auto s = static_cast<cudaStream_t>(stream);
-  const int stages = fab::default_stages(dq_fp32);
-  return D == 64 ? fab::launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                            Hkv, N, causal, stages, s, err)
-                 : fab::launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq,
-                                             Hkv, N, causal, stages, s, err);
+  return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, nullptr, 0, true, B, Hq,
+                            Hkv, N, D, causal, 0, fab::contiguous_bwd(Hq, Hkv, N, D), stream);
 }
 
 int fa_b200_device_error(int device, int reset) {

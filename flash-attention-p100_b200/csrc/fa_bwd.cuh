@@ -34,14 +34,16 @@
 namespace fab {
 
 struct BwdParams {
-  const __half* o;     // (B*Hq, N, D) forward output
-  const __half* dO;    // (B*Hq, N, D)
+  const __half* o;     // (B, Hq, N, D) forward output
+  const __half* dO;    // (B, Hq, N, D)
   const float* lse;    // (B*Hq, N) natural log
   float* dvec;         // (B*Hq, n_pad) workspace: -rowsum(dO o O) * scale
   float* lse2;         // (B*Hq, n_pad) workspace: -LSE * log2(e)
-  void* dq;            // (B*Hq, N, D) fp32 or fp16
-  __half* dk;          // (B*Hkv, N, D)
-  __half* dv;          // (B*Hkv, N, D)
+  void* dq;            // (B, Hq, N, D) fp32 or fp16
+  __half* dk;          // (B, Hkv, N, D)
+  __half* dv;          // (B, Hkv, N, D)
+  Strides so, sdo;     // element strides of o and dO (D contiguous)
+  Strides sdq, sdk, sdv;
   int* err;
   int n, n_pad, hq, group, causal;
   int dq_fp32;
@@ -58,14 +60,16 @@ __host__ __device__ constexpr int pad_rows(int n) { return (n + 127) / 128 * 128
 // shuffles.
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __restrict__ o,
+__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __restrict__ o, Strides so,
                                                               const __half* __restrict__ dO,
+                                                              Strides sdo,
                                                               const float* __restrict__ lse,
                                                               float* __restrict__ dvec,
                                                               float* __restrict__ lse2, int n,
-                                                              int n_pad, long long rows_pad,
+                                                              int n_pad, int hq, long long rows_pad,
                                                               float scale,
-                                                              float* __restrict__ dq_zero) {
+                                                              float* __restrict__ dq_zero,
+                                                              Strides sdq) {
   constexpr int TPR = D / 8;  // threads per row (8 or 16)
   const long long gtid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long prow = gtid / TPR;
@@ -73,18 +77,18 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
   const long long bh = prow / n_pad;
   const int r = static_cast<int>(prow - bh * n_pad);
   const bool real = prow < rows_pad && r < n;
-  const long long row = bh * n + r;
+  const int b = static_cast<int>(bh / hq), h = static_cast<int>(bh % hq);
   float acc = 0.f;
   if (real) {
-    if (dq_zero) {  // the fused kernel accumulates dQ into a zeroed fp32 buffer
-      float4* z = reinterpret_cast<float4*>(dq_zero + row * D) + 2 * part;
+    if (dq_zero) {  // the fused kernel accumulates dQ into a zeroed fp32 dq
+      float4* z = reinterpret_cast<float4*>(dq_zero + sdq.at(b, h, r)) + 2 * part;
       z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
       z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + row * D) + part);
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(dO + row * D) + part);
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + so.at(b, h, r)) + part);
+    const uint4 bb = __ldg(reinterpret_cast<const uint4*>(dO + sdo.at(b, h, r)) + part);
     const __half2* ha = reinterpret_cast<const __half2*>(&a);
-    const __half2* hb = reinterpret_cast<const __half2*>(&b);
+    const __half2* hb = reinterpret_cast<const __half2*>(&bb);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 fa = __half22float2(ha[i]);
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
   for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (prow < rows_pad && part == 0) {
     dvec[prow] = real ? -acc * scale : 0.f;
-    lse2[prow] = real ? __ldg(lse + row) * -1.4426950408889634f : -INFINITY;
+    lse2[prow] = real ? __ldg(lse + bh * n + r) * -1.4426950408889634f : -INFINITY;
   }
 }
 
@@ -270,25 +274,26 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(b_kv, 2 * C::TILE);
 #pragma unroll
       for (int c = 0; c < C::CH; ++c) {
-        tma_load_3d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, bkv);
-        tma_load_3d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, bkv);
+        tma_load_4d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, kvh, b);
+        tma_load_4d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, kvh, b);
       }
       int it = 0;
       bool ok = true;
       constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
       auto prefetch_step = [&](int st) {
         const int q0p = (i_start + st % nq_head) * C::BM;
-        const int bhp = b * p.hq + kvh * p.group + st / nq_head;
+        const int hqp = kvh * p.group + st / nq_head;
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_3d(&tm_q, c * 64, q0p, bhp);
-          tma_prefetch_l2_3d(&tm_do, c * 64, q0p, bhp);
+          tma_prefetch_l2_4d(&tm_q, c * 64, q0p, hqp, b);
+          tma_prefetch_l2_4d(&tm_do, c * 64, q0p, hqp, b);
         }
       };
       for (int st = 0; st < kAhead && st < total; ++st) prefetch_step(st);
       for (int step = 0; step < total && ok; ++step) {
         const int g = step / nq_head;
         const int q0 = (i_start + step % nq_head) * C::BM;
-        const int bh = b * p.hq + kvh * p.group + g;
+        const int hq_g = kvh * p.group + g;
+        const int bh = b * p.hq + hq_g;
         if (step + kAhead < total) prefetch_step(step + kAhead);
 #pragma unroll 1
         for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
@@ -300,8 +305,8 @@ __global__ void __launch_bounds__(320, 1)
           mbar_arrive_expect_tx(fb, kind ? C::TILE : C::TILE + 1024);
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
-            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
-                        c * 64, q0, bh);
+            tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
+                        c * 64, q0, hq_g, b);
           if (!kind) {
             // the Q slot of step i is released after dK_i, so slice buffer
             // i & 1 is free again by the time step i + 2 loads into it
@@ -497,15 +502,14 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const size_t rowoff = (static_cast<size_t>(bkv) * p.n + kvrow) * D;
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           const int col = w * (D / 2) + 32 * c;
           uint32_t v[32];
           tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dv + rowoff + col, v, 1.f);
+          if (kvrow < p.n) store_row32_f16(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
           tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dk + rowoff + col, v, 1.f);
+          if (kvrow < p.n) store_row32_f16(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
         }
       }
     }
@@ -589,7 +593,8 @@ __global__ void __launch_bounds__(320, 1)
   const int mb = p.causal ? (nmb - 1 - static_cast<int>(blockIdx.y)) : static_cast<int>(blockIdx.y);
   const int m0 = mb * C::BM;
   const int bh = blockIdx.x;
-  const int bkv = (bh / p.hq) * (p.hq / p.group) + (bh % p.hq) / p.group;
+  // tensor-map coordinates: batch, query head, and the kv head it reads
+  const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
   const int nblk = (p.n + C::BN - 1) / C::BN;
   const int nkv = p.causal ? min(nblk, mb + 1) : nblk;   // BM == BN
   const Ctl ctl{abort_flag, p.err};
@@ -639,36 +644,36 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(b_qdo, 2 * C::TILE);
 #pragma unroll
       for (int c = 0; c < C::CH; ++c) {
-        tma_load_3d(s_q + c * 16384, &tm_q, b_qdo, c * 64, m0, bh);
-        tma_load_3d(s_do + c * 16384, &tm_do, b_qdo, c * 64, m0, bh);
+        tma_load_4d(s_q + c * 16384, &tm_q, b_qdo, c * 64, m0, hq_i, b_i);
+        tma_load_4d(s_do + c * 16384, &tm_do, b_qdo, c * 64, m0, hq_i, b_i);
       }
       bool ok = true;
       int loaded_k = 0, loaded_v = 0;
       constexpr int kAhead = 3;  // L2 prefetch distance, in key blocks
       for (int j = 0; j < kAhead && j < nkv; ++j)
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_3d(&tm_k, c * 64, j * C::BN, bkv);
-          tma_prefetch_l2_3d(&tm_v, c * 64, j * C::BN, bkv);
+          tma_prefetch_l2_4d(&tm_k, c * 64, j * C::BN, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_v, c * 64, j * C::BN, hk_i, b_i);
         }
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + kAhead < nkv)
           for (int c = 0; c < C::CH; ++c) {
-            tma_prefetch_l2_3d(&tm_k, c * 64, (j + kAhead) * C::BN, bkv);
-            tma_prefetch_l2_3d(&tm_v, c * 64, (j + kAhead) * C::BN, bkv);
+            tma_prefetch_l2_4d(&tm_k, c * 64, (j + kAhead) * C::BN, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_v, c * 64, (j + kAhead) * C::BN, hk_i, b_i);
           }
         ok = mbar_wait(kempty(j), kph(j) ^ 1, ctl, kErrTimeoutLoad);
         if (!ok) break;
         mbar_arrive_expect_tx(kfull(j), C::TILE);
 #pragma unroll
         for (int c = 0; c < C::CH; ++c)
-          tma_load_3d(k_addr(j) + c * 16384, &tm_k, kfull(j), c * 64, j * C::BN, bkv);
+          tma_load_4d(k_addr(j) + c * 16384, &tm_k, kfull(j), c * 64, j * C::BN, hk_i, b_i);
         ++loaded_k;
         ok = mbar_wait(vempty(j), vph(j) ^ 1, ctl, kErrTimeoutLoad);
         if (!ok) break;
         mbar_arrive_expect_tx(vfull(j), C::TILE);
 #pragma unroll
         for (int c = 0; c < C::CH; ++c)
-          tma_load_3d(v_addr(j) + c * 16384, &tm_v, vfull(j), c * 64, j * C::BN, bkv);
+          tma_load_4d(v_addr(j) + c * 16384, &tm_v, vfull(j), c * 64, j * C::BN, hk_i, b_i);
         ++loaded_v;
       }
       if (!ok) {
@@ -808,7 +813,7 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const size_t rowoff = (static_cast<size_t>(bh) * p.n + row) * D;
+        const long long rowoff = p.sdq.at(b_i, hq_i, row);
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           const int col = w * (D / 2) + 32 * c;
@@ -996,25 +1001,26 @@ __global__ void __launch_bounds__(512, 1)
       mbar_arrive_expect_tx(b_kv, 2 * C::TILE);
 #pragma unroll
       for (int c = 0; c < C::CH; ++c) {
-        tma_load_3d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, bkv);
-        tma_load_3d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, bkv);
+        tma_load_4d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, kvh, b);
+        tma_load_4d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, kvh, b);
       }
       int it = 0;
       bool ok = true;
       constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
       auto prefetch_step = [&](int st) {
         const int q0p = (i_start + st % nq_head) * C::BM;
-        const int bhp = b * p.hq + kvh * p.group + st / nq_head;
+        const int hqp = kvh * p.group + st / nq_head;
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_3d(&tm_q, c * 64, q0p, bhp);
-          tma_prefetch_l2_3d(&tm_do, c * 64, q0p, bhp);
+          tma_prefetch_l2_4d(&tm_q, c * 64, q0p, hqp, b);
+          tma_prefetch_l2_4d(&tm_do, c * 64, q0p, hqp, b);
         }
       };
       for (int st = 0; st < kAhead && st < total; ++st) prefetch_step(st);
       for (int step = 0; step < total && ok; ++step) {
         const int g = step / nq_head;
         const int q0 = (i_start + step % nq_head) * C::BM;
-        const int bh = b * p.hq + kvh * p.group + g;
+        const int hq_g = kvh * p.group + g;
+        const int bh = b * p.hq + hq_g;
         if (step + kAhead < total) prefetch_step(step + kAhead);
 #pragma unroll 1
         for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
@@ -1026,8 +1032,8 @@ __global__ void __launch_bounds__(512, 1)
           mbar_arrive_expect_tx(fb, kind ? C::TILE : C::TILE + 1024);
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
-            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
-                        c * 64, q0, bh);
+            tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
+                        c * 64, q0, hq_g, b);
           if (!kind) {
             const size_t off = static_cast<size_t>(bh) * p.n_pad + q0;
             const uint32_t ls = s_lse + (step & 1) * 512;
@@ -1176,7 +1182,7 @@ __global__ void __launch_bounds__(512, 1)
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_3d(&tm_dq, box, 32 * h, row0, bh);
+          tma_reduce_add_4d(&tm_dq, box, 32 * h, row0, bh % p.hq, bh / p.hq);
           bulk_commit_group();
         }
       }
@@ -1298,15 +1304,14 @@ __global__ void __launch_bounds__(512, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const size_t rowoff = (static_cast<size_t>(bkv) * p.n + kvrow) * D;
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           const int col = w * (D / 2) + 32 * c;
           uint32_t v[32];
           tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dv + rowoff + col, v, 1.f);
+          if (kvrow < p.n) store_row32_f16(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
           tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dk + rowoff + col, v, 1.f);
+          if (kvrow < p.n) store_row32_f16(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
         }
       }
     }

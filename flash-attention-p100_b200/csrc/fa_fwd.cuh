@@ -38,7 +38,8 @@
 namespace fab {
 
 struct FwdParams {
-  __half* o;        // (B*Hq, N, D)
+  __half* o;        // (B, Hq, N, D) with strides `so` (D contiguous)
+  Strides so;
   float* lse;       // (B*Hq, N), natural log
   int* err;         // device error word
   int n;            // sequence length
@@ -126,7 +127,8 @@ __global__ void __maxnreg__(96)
   const int bh = blockIdx.x;
   const int mb = p.causal ? (p.n_mblocks - 1 - static_cast<int>(blockIdx.y)) : static_cast<int>(blockIdx.y);
   const int m0 = mb * 256;
-  const int kvh = (bh / p.hq) * (p.hq / p.group) + (bh % p.hq) / p.group;
+  // tensor-map coordinates: query head / batch, and the kv head it reads
+  const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
   const int nblk = (p.n + 127) / 128;
   int ntile[2];
 #pragma unroll
@@ -170,20 +172,20 @@ __global__ void __maxnreg__(96)
       for (int t = 0; t < 2; ++t)
 #pragma unroll
         for (int c = 0; c < C::CH; ++c)
-          tma_load_3d((t ? s_q1 : s_q0) + c * 16384, &tm_q, b_q, c * 64, m0 + 128 * t, bh);
+          tma_load_4d((t ? s_q1 : s_q0) + c * 16384, &tm_q, b_q, c * 64, m0 + 128 * t, hq_i, b_i);
       int it = 0;
       bool ok = true;
       constexpr int kAhead = 2;  // L2 prefetch distance, in key blocks
       for (int j = 0; j < kAhead && j < nkv; ++j)
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_3d(&tm_k, c * 64, j * 128, kvh);
-          tma_prefetch_l2_3d(&tm_v, c * 64, j * 128, kvh);
+          tma_prefetch_l2_4d(&tm_k, c * 64, j * 128, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_v, c * 64, j * 128, hk_i, b_i);
         }
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + kAhead < nkv)
           for (int c = 0; c < C::CH; ++c) {
-            tma_prefetch_l2_3d(&tm_k, c * 64, (j + kAhead) * 128, kvh);
-            tma_prefetch_l2_3d(&tm_v, c * 64, (j + kAhead) * 128, kvh);
+            tma_prefetch_l2_4d(&tm_k, c * 64, (j + kAhead) * 128, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_v, c * 64, (j + kAhead) * 128, hk_i, b_i);
           }
 #pragma unroll 1
         for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
@@ -196,8 +198,8 @@ __global__ void __maxnreg__(96)
           const uint32_t dst = s_ring + slot * C::KVBYTES;
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
-            tma_load_3d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
-                        c * 64, j * 128, kvh);
+            tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
+                        c * 64, j * 128, hk_i, b_i);
         }
       }
       // Drain: do not leave the CTA while a load it issued may still land.
@@ -397,8 +399,8 @@ __global__ void __maxnreg__(96)
         l += *xslot(nt & 1, hf ^ 1);
         tc_fence_after();
         const float inv = 1.f / l;
-        const size_t bhn = static_cast<size_t>(bh) * p.n;
-        __half* orow_g = p.o + (bhn + row) * D + hf * (D / 2);
+        const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
+        __half* orow_g = p.o + p.so.at(b_i, hq_i, row) + hf * (D / 2);
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           uint32_t orow[32];

@@ -25,6 +25,14 @@
 
 namespace fab {
 
+// Element strides of a (B, H, N, D) tensor whose D axis is contiguous.
+struct Strides {
+  long long b, h, n;
+  __host__ __device__ long long at(int bi, int hi, long long ni) const {
+    return bi * b + hi * h + ni * n;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // error reporting: a device-global word the host can read and clear
 // ---------------------------------------------------------------------------
@@ -161,6 +169,23 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// 4-D tiled load: coordinates are (inner column, row, head, batch); every
+// tensor the kernels read is viewed as (D, N, H, B) with arbitrary strides.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
+                                            int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_4d(const void* tmap, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // Pull a 3-D tile into L2 ahead of its real load (no shared memory, no barrier):
 // producers whose ring is too shallow to cover a DRAM round trip prefetch a
 // few steps ahead so the load into shared memory later hits L2.
@@ -191,6 +216,14 @@ __device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, uint32_t src
       "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
       " [%0, {%1, %2, %3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
       "r"(c0), "r"(c1), "r"(c2), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t src, int c0, int c1,
+                                                  int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%1, %2, %3, %4}], [%5];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {

@@ -35,9 +35,48 @@ class _FlashAttnP100(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_o):
         q, k, v, o, lse = ctx.saved_tensors
-        # dq comes back in fp32 and is cast to q's dtype (fa_p100.py:43-45)
-        dq, dk, dv = _ext.backward(q, k, v, grad_o.contiguous(), o, lse, ctx.causal)
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
+        dq, dk, dv = _grads(q, k, v, grad_o, o, lse, ctx.causal)
+        return dq, dk, dv, None, None
+
+
+def _grads(q, k, v, grad_o, o, lse, causal):
+    """dq, dk, dv in the layouts of q, k, v (so autograd needs no copies to hand
+    them on). dq is accumulated in fp32 and cast to q's dtype
+    (fa_p100.py:43-45)."""
+    dq32 = torch.empty_like(q, dtype=torch.float32)
+    dk = torch.empty_like(k, dtype=torch.float16)
+    dv = torch.empty_like(v, dtype=torch.float16)
+    _ext.backward_into(q, k, v, grad_o, o, lse, causal, torch.float32, dq32, dk, dv)
+    return dq32.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+class _FlashAttnBNHD(torch.autograd.Function):
+    """flash_attn whose output is (B, N, Hq, D) contiguous: the layout an
+    attention layer consumes next (the HF backend returns it transposed,
+    fa_p100_hf.py:142). q, k, v are (B, H, N, D) views of any layout with a
+    contiguous D axis, typically transposes of (B, N, H, D) projections; nothing
+    is copied on the way in or out, and the gradients come back in the inputs'
+    layouts."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, full_precision):
+        B, H, N, D = q.shape
+        out = torch.empty((B, N, H, D), device=q.device, dtype=torch.float16)
+        o, lse = _ext.forward(q, k, v, causal, full_precision, o=out.transpose(1, 2))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal = causal
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = _grads(q, k, v, grad_out.transpose(1, 2), o, lse, ctx.causal)
+        return dq, dk, dv, None, None
+
+
+def flash_attn_bnhd(q, k, v, causal=False, full_precision=False):
+    """flash_attn with the output laid out (B, N, Hq, D) instead of (B, Hq, N, D)."""
+    return _FlashAttnBNHD.apply(q, k, v, causal, full_precision)
 
 
 def flash_attn(q, k, v, causal=False, full_precision=False):

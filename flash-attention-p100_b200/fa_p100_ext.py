@@ -10,6 +10,12 @@ RuntimeError, as TORCH_CHECK does. Outputs and the row-sum workspace are
 allocated here with torch on the inputs' device (fa_p100_ext.cu:68-69,
 :121-124); kernels run on torch's current CUDA stream rather than the legacy
 default stream. There is no CPU path: CPU tensors are rejected.
+
+Where the reference makes every input contiguous (fa_p100_ext.cu:56, :107-108),
+these ops hand strided (B, H, N, D) views with a contiguous D axis -- e.g. the
+transposed projections an attention layer produces -- straight to the
+kernels' tensor maps; only a layout the tensor maps cannot address (an
+unaligned base or stride) is copied first.
 """
 import math
 
@@ -49,32 +55,58 @@ def _shapes(q, k, v):
     return B, H, Hkv, N, D
 
 
-def forward(q, k, v, causal, full_precision=False):
-    """O (B,Hq,N,D) fp16 and LSE (B,Hq,N) fp32 (natural log). fa_p100_ext.cu:53-83."""
+def _layout(t):
+    """(t, its fa_b200_strides), or a contiguous copy of t and its strides when
+    the tensor maps cannot address t in place."""
+    st = _lib.strides_of(t)
+    if st is None:
+        t = t.contiguous()
+        st = _lib.strides_of(t)
+    return t, st
+
+
+def _out(t, shape, dtype, device, name):
+    """A caller-supplied output (any layout the tensor maps accept) or a new
+    contiguous one."""
+    if t is None:
+        t = torch.empty(shape, device=device, dtype=dtype)
+    if tuple(t.shape) != tuple(shape) or t.dtype != dtype or t.device != device:
+        raise RuntimeError(f"{name} must be a {dtype} tensor of shape {tuple(shape)} on {device}")
+    st = _lib.strides_of(t)
+    if st is None:
+        raise RuntimeError(f"{name}: the D axis must be contiguous and the base and strides "
+                           "16-byte aligned")
+    return t, st
+
+
+def forward(q, k, v, causal, full_precision=False, o=None):
+    """O (B,Hq,N,D) fp16 and LSE (B,Hq,N) fp32 (natural log). fa_p100_ext.cu:53-83.
+    `o` may supply the output in any layout with a contiguous D axis."""
     _check_in(q, "q")
     _check_in(k, "k")
     _check_in(v, "v")
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     B, H, Hkv, N, D = _shapes(q, k, v)
-    o = torch.empty_like(q)
+    (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
+    o, so = _out(o, (B, H, N, D), torch.float16, q.device, "o")
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
-        st = _lib.lib().fa_b200_forward(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-            B, H, Hkv, N, D, 1 if causal else 0, 1 if full_precision else 0,
+        st = _lib.lib().fa_b200_forward_strided(
+            q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, o.data_ptr(), so,
+            lse.data_ptr(), B, H, Hkv, N, D, 1 if causal else 0, 1 if full_precision else 0,
             _stream_ptr(q.device))
-    _lib.check(st, "fa_b200_forward")
+    _lib.check(st, "fa_b200_forward_strided")
     return [o, lse]
 
 
-def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32):
+def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, dk=None,
+                  dv=None):
     """dq (dq_dtype), dk, dv. fp32 dq (the default, and `backward`) runs the
     fused one-pass backward, whose dq adds are not bitwise deterministic; fp16
-    dq runs the two-kernel backward (dK/dV, then dQ), which is."""
+    dq runs the two-kernel backward (dK/dV, then dQ), which is. dq, dk, dv may
+    be supplied in any layout with a contiguous D axis (new ones are
+    contiguous)."""
     _check_in(q, "q")
     _check_in(dO, "dO")
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    dO, o, lse = dO.contiguous(), o.contiguous(), lse.contiguous()
     # fa_p100_ext.cu:106-115 checks only q and dO; k, v, o and lse are checked
     # here too, because a wrong dtype would be read as garbage by the kernels.
     for t, name in ((k, "k"), (v, "v"), (o, "o")):
@@ -86,19 +118,23 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32):
         raise RuntimeError("dO and o must match q, and lse must be (B, Hq, N)")
     if dq_dtype not in (torch.float32, torch.float16):
         raise RuntimeError("dq_dtype must be float32 or float16")
-    dq = torch.empty((B, H, N, D), device=q.device, dtype=dq_dtype)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(k)
+    (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
+    (dO, sdo), (o, so) = _layout(dO), _layout(o)
+    lse = lse.contiguous()
+    dq, sdq = _out(dq, (B, H, N, D), dq_dtype, q.device, "dq")
+    dk, sdk = _out(dk, (B, Hkv, N, D), torch.float16, q.device, "dk")
+    dv, sdv = _out(dv, (B, Hkv, N, D), torch.float16, q.device, "dv")
     lib = _lib.lib()
     ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
     ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
-        st = lib.fa_b200_backward(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), dO.data_ptr(), o.data_ptr(),
-            lse.data_ptr(), dq.data_ptr(), 1 if dq_dtype == torch.float32 else 0,
-            dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes,
-            B, H, Hkv, N, D, 1 if causal else 0, _stream_ptr(q.device))
-    _lib.check(st, "fa_b200_backward")
+        st = lib.fa_b200_backward_strided(
+            q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, dO.data_ptr(), sdo,
+            o.data_ptr(), so, lse.data_ptr(), dq.data_ptr(), sdq,
+            1 if dq_dtype == torch.float32 else 0, dk.data_ptr(), sdk, dv.data_ptr(), sdv,
+            ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, 1 if causal else 0, 0,
+            _stream_ptr(q.device))
+    _lib.check(st, "fa_b200_backward_strided")
     return [dq, dk, dv]
 
 

@@ -21,7 +21,7 @@ import warnings
 
 import torch
 
-from fa_p100 import flash_attn
+from fa_p100 import flash_attn_bnhd
 
 _IMPL_NAME = "fa_p100"
 _warned_cast = False
@@ -79,9 +79,10 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
             _warned_cast = True
         query, key, value = query.half(), key.half(), value.half()
 
-    out = flash_attn(query, key, value, causal=bool(is_causal),
-                     full_precision=getattr(module, "_fa_p100_full_precision", False))
-    return out.transpose(1, 2).contiguous().to(in_dtype), None
+    # output straight in (B, N, H, D), the layout fa_p100_hf.py:142 transposes to
+    out = flash_attn_bnhd(query, key, value, causal=bool(is_causal),
+                          full_precision=getattr(module, "_fa_p100_full_precision", False))
+    return out.to(in_dtype), None
 
 
 def register():

@@ -21,6 +21,7 @@
 #define FA_B200_H_
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -48,6 +49,23 @@ enum {
 int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float* lse,
                     int B, int Hq, int Hkv, int N, int D, int causal, int full_precision,
                     void* stream);
+
+/* Element strides of a (B, H, N, D) tensor whose D axis is contiguous: the
+ * element (b, h, n, d) sits at b*batch + h*head + n*row + d. Every stride must
+ * be non-negative and a multiple of 16 bytes (8 fp16 or 4 fp32 elements). */
+typedef struct fa_b200_strides {
+  int64_t batch, head, row;
+} fa_b200_strides;
+
+/* fa_b200_forward on tensors of any strided (B, H, N, D) layout with D
+ * contiguous, e.g. (B, H, N, D) views of (B, N, H, D) storage as attention
+ * layers produce them, so the caller needs no contiguous copies; o may be
+ * strided too (lse stays (B, Hq, N) contiguous). The reference takes only
+ * contiguous tensors and copies (fa_p100_ext.cu:56); no counterpart there. */
+int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
+                            const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
+                            float* lse, int B, int Hq, int Hkv, int N, int D, int causal,
+                            int full_precision, void* stream);
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum
  * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the
@@ -92,6 +110,18 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
                             const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
                             int Hkv, int N, int D, int causal, int stages, void* stream);
+
+/* fa_b200_backward_stages on strided tensors (see fa_b200_strides): q, k, v,
+ * dO, o read and dq (fp32 or fp16), dk, dv written in their own layouts; lse
+ * and the workspace are contiguous. stages == 0 selects the default for the dq
+ * dtype. No counterpart in the reference (fa_p100_ext.cu:107-108 copies). */
+int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
+                             const void* v, fa_b200_strides sv, const void* dO,
+                             fa_b200_strides sdo, const void* o, fa_b200_strides so,
+                             const float* lse, void* dq, fa_b200_strides sdq, int dq_fp32,
+                             void* dk, fa_b200_strides sdk, void* dv, fa_b200_strides sdv,
+                             void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
+                             int N, int D, int causal, int stages, void* stream);
 
 /* Backward that allocates nothing and takes no workspace. No counterpart in
  * the reference. For callers that cannot hand the library device memory of

@@ -95,3 +95,54 @@ def test_status_strings(code):
     text = _lib.status_string(code)
     assert text and text != "unknown status"
     assert _lib.status_string(99) == "unknown status"
+
+
+def S(b=4 * 16 * 64, h=16 * 64, n=64):
+    return _lib.Strides(b, h, n)
+
+
+def fwd_strided(sq=None, so=None, o=P, D=64):
+    lib = _lib.lib()
+    sq = sq or S()
+    return lib.fa_b200_forward_strided(P, sq, P, S(2 * 16 * 64), P, S(2 * 16 * 64), o, so or S(),
+                                       P, 1, 4, 2, 16, D, 1, 0, None)
+
+
+def test_strided_forward_argument_errors():
+    # strides must be non-negative multiples of 16 bytes (8 fp16 elements)
+    assert fwd_strided(sq=S(n=68)) == 4
+    assert fwd_strided(sq=S(h=-64)) == 4
+    assert fwd_strided(so=S(b=4 * 16 * 64 + 4)) == 4
+    assert fwd_strided(o=MISALIGNED) == 4
+    assert fwd_strided(D=96) == 2
+
+
+def bwd_strided(sdq=None, dq_fp32=1, stages=0, **kw):
+    lib = _lib.lib()
+    sq, skv = S(), S(2 * 16 * 64)
+    return lib.fa_b200_backward_strided(
+        P, sq, P, skv, P, skv, P, sq, P, sq, P, P, sdq or S(), dq_fp32, P, skv, P, skv,
+        P, 1 << 20, 1, 4, 2, 16, 64, 1, stages, None)
+
+
+def test_strided_backward_argument_errors():
+    # an fp32 dq needs strides in multiples of 4 elements, fp16 ones of 8
+    assert bwd_strided(sdq=S(n=66)) == 4
+    assert bwd_strided(sdq=S(n=68), dq_fp32=0) == 4
+    assert bwd_strided(stages=8, dq_fp32=0) == 3     # the fused stage needs an fp32 dq
+    assert bwd_strided(stages=64) == 3
+
+
+def test_strides_of_layouts():
+    import torch
+    # (B, H, N, D) view of (B, N, H, D) storage, as attention layers produce it
+    t = torch.empty(2, 8192, 16, 128, dtype=torch.float16).transpose(1, 2)
+    st = _lib.strides_of(t)
+    assert (st.batch, st.head, st.row) == (8192 * 16 * 128, 128, 16 * 128)
+    # size-1 dimensions take the contiguous stride whatever torch reports
+    t1 = torch.empty(1, 8192, 16, 128, dtype=torch.float16).transpose(1, 2)
+    assert _lib.strides_of(t1).batch == 16 * 8192 * 128
+    # a non-contiguous D axis or an unaligned row stride does not qualify
+    assert _lib.strides_of(torch.empty(1, 2, 16, 64, dtype=torch.float16).transpose(2, 3)) is None
+    assert _lib.strides_of(torch.empty(1, 2, 16, 68, dtype=torch.float16)[..., :64]) is None
+    assert _lib.strides_of(torch.empty(1, 2, 16, 72, dtype=torch.float16)[..., :64]) is not None
