@@ -26,10 +26,10 @@ _S = Strides
 SIGNATURES = {
     "fa_b200_forward": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_forward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P,
-                                     _I, _I, _I, _I, _I, _I, _I, _P]),
+                                     _I, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P,
                                       _P, _S, _I, _P, _S, _P, _S, _P, _SZ,
-                                      _I, _I, _I, _I, _I, _I, _I, _P]),
+                                      _I, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_workspace_bytes": (_SZ, [_I, _I, _I]),
     "fa_b200_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                               _I, _I, _I, _I, _I, _I, _P]),
@@ -43,6 +43,9 @@ SIGNATURES = {
     "fa_b200_last_error": (ctypes.c_char_p, []),
     "fa_b200_selftest_gemm": (_I, [_P, _P, _P, _I, _I, _I, _P]),
 }
+
+# FA_B200_DTYPE_* of the 16-bit tensors of the strided entry points
+DTYPE_FP16, DTYPE_BF16 = 0, 1
 
 _lib = None
 

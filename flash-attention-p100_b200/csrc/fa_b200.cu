@@ -72,6 +72,20 @@ void set_smem(K kernel, int bytes) {
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Opt every kernel of one element type (fp16, or bf16 when BF) in to its
+// dynamic shared memory.
+template <bool BF>
+void set_smem_all() {
+  set_smem(fwd_kernel<64, BF>, FwdCfg<64>::SMEM);
+  set_smem(fwd_kernel<128, BF>, FwdCfg<128>::SMEM);
+  set_smem(bwd_dkdv_kernel<64, BF>, DkdvCfg<64>::SMEM);
+  set_smem(bwd_dkdv_kernel<128, BF>, DkdvCfg<128>::SMEM);
+  set_smem(bwd_dq_kernel<64, BF>, DqCfg<64>::SMEM);
+  set_smem(bwd_dq_kernel<128, BF>, DqCfg<128>::SMEM);
+  set_smem(bwd_fused_kernel<64, BF>, FusedCfg<64>::SMEM);
+  set_smem(bwd_fused_kernel<128, BF>, FusedCfg<128>::SMEM);
+}
+
 // One-time, per-device set-up with that device current: architecture check,
 // opt-in to large dynamic shared memory, and the error word's address.
 int device_setup(int* dev_out, int** err_out) {
@@ -103,14 +117,8 @@ int device_setup(int* dev_out, int** err_out) {
         st.status = FA_B200_ERR_DEVICE;
       } else {
         st.err = static_cast<int*>(addr);
-        set_smem(fwd_kernel<64>, FwdCfg<64>::SMEM);
-        set_smem(fwd_kernel<128>, FwdCfg<128>::SMEM);
-        set_smem(bwd_dkdv_kernel<64>, DkdvCfg<64>::SMEM);
-        set_smem(bwd_dkdv_kernel<128>, DkdvCfg<128>::SMEM);
-        set_smem(bwd_dq_kernel<64>, DqCfg<64>::SMEM);
-        set_smem(bwd_dq_kernel<128>, DqCfg<128>::SMEM);
-        set_smem(bwd_fused_kernel<64>, FusedCfg<64>::SMEM);
-        set_smem(bwd_fused_kernel<128>, FusedCfg<128>::SMEM);
+        set_smem_all<false>();
+        set_smem_all<true>();
         st.status = (cudaGetLastError() == cudaSuccess) ? FA_B200_OK : FA_B200_ERR_DEVICE;
       }
     }
@@ -226,18 +234,19 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
   return FA_B200_OK;
 }
 
-template <int D>
+template <int D, bool BF>
 int launch_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
                    int Hkv, int N, int causal, const FwdLayout& L, cudaStream_t stream, int* err) {
   using C = FwdCfg<D>;
   CUtensorMap tq, tk, tv;
   const uint64_t BH = static_cast<uint64_t>(B) * Hq;
-  if (!make_map4(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.q, 128) ||
-      !make_map4(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.k, 128) ||
-      !make_map4(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.v, 128))
+  const CUtensorMapDataType dt = BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (!make_map4(&tq, q, dt, 2, D, N, Hq, B, L.q, 128) ||
+      !make_map4(&tk, k, dt, 2, D, N, Hkv, B, L.k, 128) ||
+      !make_map4(&tv, v, dt, 2, D, N, Hkv, B, L.v, 128))
     return FA_B200_ERR_TENSOR_MAP;
   FwdParams p;
-  p.o = static_cast<__half*>(o);
+  p.o = static_cast<uint16_t*>(o);
   p.so = L.o;
   p.lse = lse;
   p.err = err;
@@ -249,11 +258,11 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
   if (p.n_mblocks > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
   dim3 grid(static_cast<unsigned>(BH), p.n_mblocks);
-  fwd_kernel<D><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
+  fwd_kernel<D, BF><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
   return launch_status("fwd_kernel");
 }
 
-template <int D>
+template <int D, bool BF>
 int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
                     const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* ws, int B,
                     int Hq, int Hkv, int N, int causal, int stages, const BwdLayout& L,
@@ -263,14 +272,15 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
   // Every operand tile of the gradient kernels is 128 rows.
   CUtensorMap tq, tdo, tk, tv;
-  if (!make_map4(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.q, 128) ||
-      !make_map4(&tdo, dO, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hq, B, L.dO, 128) ||
-      !make_map4(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.k, 128) ||
-      !make_map4(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, D, N, Hkv, B, L.v, 128))
+  const CUtensorMapDataType dt = BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (!make_map4(&tq, q, dt, 2, D, N, Hq, B, L.q, 128) ||
+      !make_map4(&tdo, dO, dt, 2, D, N, Hq, B, L.dO, 128) ||
+      !make_map4(&tk, k, dt, 2, D, N, Hkv, B, L.k, 128) ||
+      !make_map4(&tv, v, dt, 2, D, N, Hkv, B, L.v, 128))
     return FA_B200_ERR_TENSOR_MAP;
   BwdParams p;
-  p.o = static_cast<const __half*>(o);
-  p.dO = static_cast<const __half*>(dO);
+  p.o = static_cast<const uint16_t*>(o);
+  p.dO = static_cast<const uint16_t*>(dO);
   p.so = L.o;
   p.sdo = L.dO;
   p.sdq = L.dq;
@@ -283,8 +293,8 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   p.lse2 = ws + rows_pad;
   p.n_pad = n_pad;
   p.dq = dq;
-  p.dk = static_cast<__half*>(dk);
-  p.dv = static_cast<__half*>(dv);
+  p.dk = static_cast<uint16_t*>(dk);
+  p.dv = static_cast<uint16_t*>(dv);
   p.err = err;
   p.n = N;
   p.hq = Hq;
@@ -296,14 +306,14 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
 
   if (stages & FA_B200_STAGE_ROWSUM) {
     const long long threads = rows_pad * (D / 8);
-    bwd_preprocess_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        static_cast<const __half*>(o), L.o, static_cast<const __half*>(dO), L.dO, lse, p.dvec,
+    bwd_preprocess_kernel<D, BF><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(o), L.o, static_cast<const uint16_t*>(dO), L.dO, lse, p.dvec,
         p.lse2, N, n_pad, Hq, rows_pad, p.scale, p.dq_fp32 ? static_cast<float*>(dq) : nullptr,
         L.dq);
     if (int st = launch_status("bwd_preprocess_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DKDV) {
-    bwd_dkdv_kernel<D><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
+    bwd_dkdv_kernel<D, BF><<<dim3(static_cast<unsigned>(BHkv), nq128), DkdvCfg<D>::THREADS,
                          DkdvCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, p);
     if (int st = launch_status("bwd_dkdv_kernel")) return st;
   }
@@ -320,12 +330,12 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const uint64_t n_groups = (BHkv + hg_max - 1) / hg_max;
     p.head_group = static_cast<int>((BHkv + n_groups - 1) / n_groups);
     if (BHkv * static_cast<uint64_t>(nq128) > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-    bwd_fused_kernel<D><<<static_cast<unsigned>(BHkv * nq128), FusedCfg<D>::THREADS,
+    bwd_fused_kernel<D, BF><<<static_cast<unsigned>(BHkv * nq128), FusedCfg<D>::THREADS,
                           FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
     if (int st = launch_status("bwd_fused_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DQ) {
-    bwd_dq_kernel<D><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
+    bwd_dq_kernel<D, BF><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
                        stream>>>(tq, tk, tv, tdo, p);
     if (int st = launch_status("bwd_dq_kernel")) return st;
   }
@@ -447,10 +457,11 @@ namespace {
 Strides from_abi(fa_b200_strides st) { return Strides{st.batch, st.head, st.row}; }
 
 int forward_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                 int Hkv, int N, int D, int causal, const FwdLayout& L, void* stream) {
+                 int Hkv, int N, int D, int dtype, int causal, const FwdLayout& L, void* stream) {
   if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
   int st = check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
+  if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(lse) ||
       !strides_ok(L.q, 2) || !strides_ok(L.k, 2) || !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
     return FA_B200_ERR_ALIGNMENT;
@@ -459,15 +470,19 @@ int forward_impl(const void* q, const void* k, const void* v, void* o, float* ls
   st = device_setup(&dev, &err);
   if (st != FA_B200_OK) return st;
   auto s = static_cast<cudaStream_t>(stream);
-  return D == 64 ? launch_forward<64>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
-                 : launch_forward<128>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
+  const bool bf = dtype == FA_B200_DTYPE_BF16;
+  if (D == 64)
+    return bf ? launch_forward<64, true>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
+              : launch_forward<64, false>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
+  return bf ? launch_forward<128, true>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
+            : launch_forward<128, false>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
 }
 
 // ws == nullptr: the built-in scratch of fa_b200_backward_noalloc.
 int backward_impl(const void* q, const void* k, const void* v, const void* dO, const void* o,
                   const float* lse, void* dq, int dq_fp32, void* dk, void* dv, void* workspace,
                   size_t workspace_bytes, bool noalloc, int B, int Hq, int Hkv, int N, int D,
-                  int causal, int stages, const BwdLayout& L, void* stream) {
+                  int dtype, int causal, int stages, const BwdLayout& L, void* stream) {
   if (stages == 0) stages = default_stages(dq_fp32);
   if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
   if ((stages & FA_B200_STAGE_FUSED) && (!dq_fp32 || (stages & (FA_B200_STAGE_DKDV | FA_B200_STAGE_DQ))))
@@ -475,6 +490,7 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
   if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
   int st = check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
+  if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
   if (noalloc) {
     const size_t rows = static_cast<size_t>(B) * Hq * pad_rows(N);
     if (rows > kNoAllocRows) {
@@ -502,10 +518,13 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
   float* ws = noalloc ? noalloc_scratch(dev) : static_cast<float*>(workspace);
   if (!ws) return FA_B200_ERR_DEVICE;
   auto s = static_cast<cudaStream_t>(stream);
-  return D == 64 ? launch_backward<64>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv, N,
-                                       causal, stages, L, s, err)
-                 : launch_backward<128>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv,
-                                        N, causal, stages, L, s, err);
+  const bool bf = dtype == FA_B200_DTYPE_BF16;
+#define FAB_BWD(DD, BB)                                                                     \
+  launch_backward<DD, BB>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv, N, causal, \
+                          stages, L, s, err)
+  if (D == 64) return bf ? FAB_BWD(64, true) : FAB_BWD(64, false);
+  return bf ? FAB_BWD(128, true) : FAB_BWD(128, false);
+#undef FAB_BWD
 }
 
 BwdLayout contiguous_bwd(int Hq, int Hkv, int N, int D) {
@@ -525,16 +544,16 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
                     int Hkv, int N, int D, int causal, int full_precision, void* stream) {
   (void)full_precision;
   const fab::Strides sq = fab::contiguous(Hq, N, D), skv = fab::contiguous(Hkv, N, D);
-  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, causal,
+  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, FA_B200_DTYPE_FP16, causal,
                            fab::FwdLayout{sq, skv, skv, sq}, stream);
 }
 
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
-                            float* lse, int B, int Hq, int Hkv, int N, int D, int causal,
-                            int full_precision, void* stream) {
+                            float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
+                            int causal, int full_precision, void* stream) {
   (void)full_precision;
-  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, causal,
+  return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, dtype, causal,
                            fab::FwdLayout{fab::from_abi(sq), fab::from_abi(sk), fab::from_abi(sv),
                                           fab::from_abi(so)},
                            stream);
@@ -552,7 +571,7 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream) {
   return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
-                            false, B, Hq, Hkv, N, D, causal, 0,
+                            false, B, Hq, Hkv, N, D, FA_B200_DTYPE_FP16, causal, 0,
                             fab::contiguous_bwd(Hq, Hkv, N, D), stream);
 }
 
@@ -562,7 +581,7 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
                             int Hkv, int N, int D, int causal, int stages, void* stream) {
   if (stages == 0) return FA_B200_ERR_SHAPE;
   return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
-                            false, B, Hq, Hkv, N, D, causal, stages,
+                            false, B, Hq, Hkv, N, D, FA_B200_DTYPE_FP16, causal, stages,
                             fab::contiguous_bwd(Hq, Hkv, N, D), stream);
 }
 
@@ -572,10 +591,10 @@ int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, f
                              const float* lse, void* dq, fa_b200_strides sdq, int dq_fp32,
                              void* dk, fa_b200_strides sdk, void* dv, fa_b200_strides sdv,
                              void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
-                             int N, int D, int causal, int stages, void* stream) {
+                             int N, int D, int dtype, int causal, int stages, void* stream) {
   using fab::from_abi;
   return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, workspace, workspace_bytes,
-                            false, B, Hq, Hkv, N, D, causal, stages,
+                            false, B, Hq, Hkv, N, D, dtype, causal, stages,
                             fab::BwdLayout{from_abi(sq), from_abi(sk), from_abi(sv), from_abi(sdo),
                                            from_abi(so), from_abi(sdq), from_abi(sdk),
                                            from_abi(sdv)},
@@ -589,7 +608,8 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
                              void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
                              void* stream) {
   return fab::backward_impl(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, nullptr, 0, true, B, Hq,
-                            Hkv, N, D, causal, 0, fab::contiguous_bwd(Hq, Hkv, N, D), stream);
+                            Hkv, N, D, FA_B200_DTYPE_FP16, causal, 0,
+                            fab::contiguous_bwd(Hq, Hkv, N, D), stream);
 }
 
 int fa_b200_device_error(int device, int reset) {
@@ -618,6 +638,7 @@ const char* fa_b200_status_string(int status) {
     case FA_B200_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled rejected a tensor";
     case FA_B200_ERR_LAUNCH: return "kernel launch failed";
     case FA_B200_ERR_WORKSPACE: return "workspace missing or too small";
+    case FA_B200_ERR_DTYPE: return "dtype must be FA_B200_DTYPE_FP16 or FA_B200_DTYPE_BF16";
     case FA_B200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FA_B200_ERR_TOO_LARGE: return "problem exceeds a CUDA grid limit";
     case FA_B200_ERR_SCRATCH_LIMIT: return "problem exceeds the built-in scratch of the no-allocation backward";

@@ -34,14 +34,14 @@
 namespace fab {
 
 struct BwdParams {
-  const __half* o;     // (B, Hq, N, D) forward output
-  const __half* dO;    // (B, Hq, N, D)
+  const uint16_t* o;   // (B, Hq, N, D) forward output (fp16 or bf16, as all the
+  const uint16_t* dO;  // (B, Hq, N, D)          16-bit tensors of one call)
   const float* lse;    // (B*Hq, N) natural log
   float* dvec;         // (B*Hq, n_pad) workspace: -rowsum(dO o O) * scale
   float* lse2;         // (B*Hq, n_pad) workspace: -LSE * log2(e)
   void* dq;            // (B, Hq, N, D) fp32 or fp16
-  __half* dk;          // (B, Hkv, N, D)
-  __half* dv;          // (B, Hkv, N, D)
+  uint16_t* dk;        // (B, Hkv, N, D)
+  uint16_t* dv;        // (B, Hkv, N, D)
   Strides so, sdo;     // element strides of o and dO (D contiguous)
   Strides sdq, sdk, sdv;
   int* err;
@@ -59,9 +59,9 @@ __host__ __device__ constexpr int pad_rows(int n) { return (n + 127) / 128 * 128
 // HBM-bound, one 16-byte vector per thread, D/8 threads per row reduced with
 // shuffles.
 // ---------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __restrict__ o, Strides so,
-                                                              const __half* __restrict__ dO,
+template <int D, bool BF>
+__global__ void __launch_bounds__(256) bwd_preprocess_kernel(const uint16_t* __restrict__ o, Strides so,
+                                                              const uint16_t* __restrict__ dO,
                                                               Strides sdo,
                                                               const float* __restrict__ lse,
                                                               float* __restrict__ dvec,
@@ -87,12 +87,11 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
     }
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(o + so.at(b, h, r)) + part);
     const uint4 bb = __ldg(reinterpret_cast<const uint4*>(dO + sdo.at(b, h, r)) + part);
-    const __half2* ha = reinterpret_cast<const __half2*>(&a);
-    const __half2* hb = reinterpret_cast<const __half2*>(&bb);
+    const uint32_t ha[4] = {a.x, a.y, a.z, a.w}, hb[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 fa = __half22float2(ha[i]);
-      const float2 fb = __half22float2(hb[i]);
+      const float2 fa = unpack2<BF>(ha[i]);
+      const float2 fb = unpack2<BF>(hb[i]);
       acc = fmaf(fa.x, fb.x, acc);
       acc = fmaf(fa.y, fb.y, acc);
     }
@@ -106,14 +105,16 @@ __global__ void __launch_bounds__(256) bwd_preprocess_kernel(const __half* __res
 }
 
 // Write 32 fp32 values as fp16 / fp32 to global, 16 bytes per store.
-__device__ __forceinline__ void store_row32_f16(__half* dst, const uint32_t (&v)[32], float mul) {
+// (16-bit: fp16, or bf16 when BF)
+template <bool BF>
+__device__ __forceinline__ void store_row32_h(uint16_t* dst, const uint32_t (&v)[32], float mul) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint4 pk;
-    pk.x = pack_half2(__uint_as_float(v[8 * q + 0]) * mul, __uint_as_float(v[8 * q + 1]) * mul);
-    pk.y = pack_half2(__uint_as_float(v[8 * q + 2]) * mul, __uint_as_float(v[8 * q + 3]) * mul);
-    pk.z = pack_half2(__uint_as_float(v[8 * q + 4]) * mul, __uint_as_float(v[8 * q + 5]) * mul);
-    pk.w = pack_half2(__uint_as_float(v[8 * q + 6]) * mul, __uint_as_float(v[8 * q + 7]) * mul);
+    pk.x = pack2<BF>(__uint_as_float(v[8 * q + 0]) * mul, __uint_as_float(v[8 * q + 1]) * mul);
+    pk.y = pack2<BF>(__uint_as_float(v[8 * q + 2]) * mul, __uint_as_float(v[8 * q + 3]) * mul);
+    pk.z = pack2<BF>(__uint_as_float(v[8 * q + 4]) * mul, __uint_as_float(v[8 * q + 5]) * mul);
+    pk.w = pack2<BF>(__uint_as_float(v[8 * q + 6]) * mul, __uint_as_float(v[8 * q + 7]) * mul);
     reinterpret_cast<uint4*>(dst)[q] = pk;
   }
 }
@@ -137,13 +138,14 @@ __device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]
 
 // Thread-row r writes 32 fp16 values (columns 32*half .. +31 of a 64-column
 // K-major swizzled tile of 128 rows) as four 16-byte pieces.
+template <bool BF>
 __device__ __forceinline__ void st_row32_sw128(uint32_t tile, int r, int half, const float (&x)[32]) {
 #pragma unroll
   for (int c4 = 0; c4 < 4; ++c4) {
     const int piece = 4 * half + c4;
-    st_shared_v4(tile + r * 128 + ((piece ^ (r & 7)) << 4), pack_half2(x[8 * c4], x[8 * c4 + 1]),
-                 pack_half2(x[8 * c4 + 2], x[8 * c4 + 3]), pack_half2(x[8 * c4 + 4], x[8 * c4 + 5]),
-                 pack_half2(x[8 * c4 + 6], x[8 * c4 + 7]));
+    st_shared_v4(tile + r * 128 + ((piece ^ (r & 7)) << 4), pack2<BF>(x[8 * c4], x[8 * c4 + 1]),
+                 pack2<BF>(x[8 * c4 + 2], x[8 * c4 + 3]), pack2<BF>(x[8 * c4 + 4], x[8 * c4 + 5]),
+                 pack2<BF>(x[8 * c4 + 6], x[8 * c4 + 7]));
   }
 }
 
@@ -155,12 +157,13 @@ namespace fab {
 
 // Store 64 fp32 values as 32 packed fp16 pairs into TMEM columns [col, col+32)
 // of this warp's lanes (the A-operand layout: column c holds elements 2c, 2c+1).
+template <bool BF>
 __device__ __forceinline__ void tmem_st_pairs(uint32_t taddr, const float (&x)[2][32]) {
   uint32_t v[32];
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     const int h = c >> 4, e = 2 * (c & 15);
-    v[c] = pack_half2(x[h][e], x[h][e + 1]);
+    v[c] = pack2<BF>(x[h][e], x[h][e + 1]);
   }
   tmem_st32(taddr, v);
 }
@@ -209,7 +212,7 @@ struct DkdvCfg {
   static constexpr uint32_t COL_DS = 160;
 };
 
-template <int D>
+template <int D, bool BF>
 __global__ void __launch_bounds__(320, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -325,8 +328,8 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
-      constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV (SS), dK (TS)
+      constexpr uint32_t id_t = idesc_f16(128, 128, false, false, BF);  // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true, BF);     // dV (SS), dK (TS)
       // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
         const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
@@ -465,8 +468,8 @@ __global__ void __launch_bounds__(320, 1)
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
       }
-      st_row32_sw128(s_p + w * 16384, r, 0, pv[0]);
-      st_row32_sw128(s_p + w * 16384, r, 1, pv[1]);
+      st_row32_sw128<BF>(s_p + w * 16384, r, 0, pv[0]);
+      st_row32_sw128<BF>(s_p + w * 16384, r, 1, pv[1]);
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(b_p);
@@ -492,7 +495,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int e4 = 0; e4 < 4; ++e4)
             pv[h][4 * c4 + e4] *= fmaf(__uint_as_float(sr[h][4 * c4 + e4]), p.scale, dv[e4]);
         }
-      tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
+      tmem_st_pairs<BF>(tmem + C::COL_DS + 32 * w + lane_off, pv);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_ds);
@@ -507,9 +510,9 @@ __global__ void __launch_bounds__(320, 1)
           const int col = w * (D / 2) + 32 * c;
           uint32_t v[32];
           tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
+          if (kvrow < p.n) store_row32_h<BF>(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
           tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
+          if (kvrow < p.n) store_row32_h<BF>(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
         }
       }
     }
@@ -568,7 +571,7 @@ struct DqCfg {
   static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256, COL_DS = 384;
 };
 
-template <int D>
+template <int D, bool BF>
 __global__ void __launch_bounds__(320, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -685,8 +688,8 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nkv > 0) {
-      constexpr uint32_t id_s = idesc_f16(128, 128, false, false);
-      constexpr uint32_t id_q = idesc_f16(128, D, false, true);
+      constexpr uint32_t id_s = idesc_f16(128, 128, false, false, BF);
+      constexpr uint32_t id_q = idesc_f16(128, D, false, true, BF);
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
         const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
 #pragma unroll
@@ -803,7 +806,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c) pv[h][c] *= fmaf(__uint_as_float(sr[h][c]), p.scale, ndvs);
-      tmem_st_pairs(tmem + C::COL_DS + 64 * (j & 1) + 32 * w + lane_off, pv);
+      tmem_st_pairs<BF>(tmem + C::COL_DS + 64 * (j & 1) + 32 * w + lane_off, pv);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_ds + 8 * (j & 1));
@@ -823,7 +826,7 @@ __global__ void __launch_bounds__(320, 1)
             if (p.dq_fp32)
               store_row32_f32(static_cast<float*>(p.dq) + rowoff + col, v, 1.f);
             else
-              store_row32_f16(static_cast<__half*>(p.dq) + rowoff + col, v, 1.f);
+              store_row32_h<BF>(static_cast<uint16_t*>(p.dq) + rowoff + col, v, 1.f);
           }
         }
       }
@@ -919,7 +922,7 @@ struct FusedCfg {
   static constexpr uint32_t COL_P = 32, COL_DS = 160, COL_DQ = DQ_OWN_COLS ? 384 : 128;
 };
 
-template <int D>
+template <int D, bool BF>
 __global__ void __launch_bounds__(512, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -1050,9 +1053,9 @@ __global__ void __launch_bounds__(512, 1)
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
-      constexpr uint32_t id_t = idesc_f16(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true);     // dV, dK (TS)
-      constexpr uint32_t id_q = idesc_f16(128, D, true, true);      // dQ: A = dS MN-major
+      constexpr uint32_t id_t = idesc_f16(128, 128, false, false, BF);  // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true, BF);     // dV, dK (TS)
+      constexpr uint32_t id_q = idesc_f16(128, D, true, true, BF);      // dQ: A = dS MN-major
       // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
         const uint64_t da = sdesc_sw128(a_s, 16, 1024), db = sdesc_sw128(b_s_, 16, 1024);
@@ -1243,7 +1246,7 @@ __global__ void __launch_bounds__(512, 1)
             if (q < qlim || q >= p.n) pv[h][c] = 0.f;
           }
       }
-      tmem_st_pairs(tmem + C::COL_P + 32 * w + lane_off, pv);
+      tmem_st_pairs<BF>(tmem + C::COL_P + 32 * w + lane_off, pv);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p);
@@ -1283,9 +1286,9 @@ __global__ void __launch_bounds__(512, 1)
           }
         }
       // dS^T as fp16 pairs over dP^T columns this group has read (A of dK)
-      tmem_st_pairs(tmem + C::COL_DS + 32 * w + lane_off, pv);
-      st_row32_sw128(s_ds + w * 16384, r, 0, pv[0]);
-      st_row32_sw128(s_ds + w * 16384, r, 1, pv[1]);
+      tmem_st_pairs<BF>(tmem + C::COL_DS + 32 * w + lane_off, pv);
+      st_row32_sw128<BF>(s_ds + w * 16384, r, 0, pv[0]);
+      st_row32_sw128<BF>(s_ds + w * 16384, r, 1, pv[1]);
       fence_async_smem();
       tmem_st_wait();
       tc_fence_before();
@@ -1309,9 +1312,9 @@ __global__ void __launch_bounds__(512, 1)
           const int col = w * (D / 2) + 32 * c;
           uint32_t v[32];
           tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
+          if (kvrow < p.n) store_row32_h<BF>(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
           tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-          if (kvrow < p.n) store_row32_f16(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
+          if (kvrow < p.n) store_row32_h<BF>(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
         }
       }
     }

@@ -38,7 +38,7 @@
 namespace fab {
 
 struct FwdParams {
-  __half* o;        // (B, Hq, N, D) with strides `so` (D contiguous)
+  uint16_t* o;      // (B, Hq, N, D) fp16 or bf16, strides `so` (D contiguous)
   Strides so;
   float* lse;       // (B*Hq, N), natural log
   int* err;         // device error word
@@ -81,9 +81,9 @@ namespace fab {
 // MMA issue helpers (single thread)
 // ---------------------------------------------------------------------------
 // S[tmem] = Q_tile (128 x D, K-major) * K_tile^T (128 x D, K-major)
-template <int D>
+template <int D, bool BF>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t k_s) {
-  constexpr uint32_t idesc = idesc_f16(128, 128, false, false);
+  constexpr uint32_t idesc = idesc_f16(128, 128, false, false, BF);
   const uint64_t dq = sdesc_sw128(q_s, 16, 1024), dk = sdesc_sw128(k_s, 16, 1024);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
@@ -92,10 +92,10 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t
   }
 }
 // O[tmem] (+)= P (128 x 128 keys, fp16 pairs in TMEM) * V (128 keys x D, MN-major)
-template <int D>
+template <int D, bool BF>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_s,
                                          bool accumulate) {
-  constexpr uint32_t idesc = idesc_f16(128, D, false, true);
+  constexpr uint32_t idesc = idesc_f16(128, D, false, true, BF);
   const uint64_t dv = sdesc_sw128(v_s, 16384, 1024);
 #pragma unroll
   for (int kk = 0; kk < 128 / 16; ++kk)
@@ -103,7 +103,7 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
            (accumulate || kk > 0) ? 1u : 0u);
 }
 
-template <int D>
+template <int D, bool BF>
 __global__ void __maxnreg__(96)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
@@ -221,7 +221,7 @@ __global__ void __maxnreg__(96)
 #pragma unroll
           for (int t = 0; t < 2; ++t)
             if (ntile[t] > 0) {
-              issue_qk<D>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0, s_ring);
+              issue_qk<D, BF>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0, s_ring);
               mma_commit(b_s + 8 * t);
             }
           mma_commit(b_empty);
@@ -245,7 +245,7 @@ __global__ void __maxnreg__(96)
           ok = mbar_wait(b_p + 8 * t, j & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_pv<D>(tmem + (t ? C::COL_O1 : C::COL_O0),
+          issue_pv<D, BF>(tmem + (t ? C::COL_O1 : C::COL_O0),
                       tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P, s_ring + slot_v * C::KVBYTES,
                       j > 0);
           if (j + 1 < ntile[t]) {
@@ -255,7 +255,7 @@ __global__ void __maxnreg__(96)
               tc_fence_after();
               have_k = true;
             }
-            issue_qk<D>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0,
+            issue_qk<D, BF>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0,
                         s_ring + slot_k * C::KVBYTES);
             mma_commit(b_s + 8 * t);
           } else {
@@ -366,7 +366,7 @@ __global__ void __maxnreg__(96)
               f32x2_split(fma_x2(f32x2(s[32 * c32 + 2 * h], s[32 * c32 + 2 * h + 1]), sl2, nm));
           const float e0 = ex2(x.x), e1 = ex2(x.y);
           lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
-          w[h] = pack_half2(e0, e1);
+          w[h] = pack2<BF>(e0, e1);
         }
         tmem_st16(t_s + C::COL_P + 32 * hf + 16 * c32, w);
       }
@@ -400,7 +400,7 @@ __global__ void __maxnreg__(96)
         tc_fence_after();
         const float inv = 1.f / l;
         const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
-        __half* orow_g = p.o + p.so.at(b_i, hq_i, row) + hf * (D / 2);
+        uint16_t* orow_g = p.o + p.so.at(b_i, hq_i, row) + hf * (D / 2);
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           uint32_t orow[32];
@@ -410,10 +410,10 @@ __global__ void __maxnreg__(96)
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
               uint4 pk;
-              pk.x = pack_half2(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
-              pk.y = pack_half2(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
-              pk.z = pack_half2(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
-              pk.w = pack_half2(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
+              pk.x = pack2<BF>(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
+              pk.y = pack2<BF>(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
+              pk.z = pack2<BF>(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
+              pk.w = pack2<BF>(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
               *reinterpret_cast<uint4*>(orow_g + 32 * c + 8 * v) = pk;
             }
           }

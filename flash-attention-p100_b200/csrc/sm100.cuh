@@ -21,6 +21,7 @@
 // TMEM column n (fp32). Warp w of a CTA may only touch lanes 32*(w%4)..+31.
 #pragma once
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace fab {
@@ -276,11 +277,12 @@ __device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_off) 
   return desc + (byte_off >> 4);
 }
 
-// Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulation.
-// a_mn / b_mn select MN-major (transposed) operands.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn) {
+// Instruction descriptor for kind::f16 with fp32 accumulation; A and B both
+// fp16 or (bf) both bf16. a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn,
+                                                 bool bf = false) {
   return (1u << 4)                                    // D format: f32
-         | (0u << 7) | (0u << 10)                     // A, B: f16
+         | ((bf ? 1u : 0u) << 7) | ((bf ? 1u : 0u) << 10)   // A, B: f16 (0) or bf16 (1)
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
          | (static_cast<uint32_t>(N >> 3) << 17)      // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);     // M / 16
@@ -421,6 +423,22 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Two fp32 values rounded to the 16-bit element type (fp16, or bf16 when BF),
+// low half first; and back.
+template <bool BF>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF) return pack_bf162(lo, hi);
+  else return pack_half2(lo, hi);
+}
+template <bool BF>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (BF) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  else return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {

@@ -7,7 +7,8 @@ SIMT kernels replaced by tcgen05 tensor-core kernels in libfa_b200.so.
     from fa_p100 import flash_attn
     o = flash_attn(q, k, v, causal=True)   # q (B,Hq,N,D), k/v (B,Hkv,N,D), fp16 CUDA
 
-D is 64 or 128, N is arbitrary, Hq a multiple of Hkv (MHA, GQA, MQA).
+D is 64 or 128, N is arbitrary, Hq a multiple of Hkv (MHA, GQA, MQA). The
+tensors are fp16 (the reference's type) or, beyond it, bf16.
 `full_precision` is accepted and ignored: the tensor cores multiply fp16
 exactly and accumulate in fp32, which is the reference's fp32-MAC tier.
 The backward follows the reference's flow: dq in fp32 (accumulated across key
@@ -44,8 +45,8 @@ def _grads(q, k, v, grad_o, o, lse, causal):
     them on). dq is accumulated in fp32 and cast to q's dtype
     (fa_p100.py:43-45)."""
     dq32 = torch.empty_like(q, dtype=torch.float32)
-    dk = torch.empty_like(k, dtype=torch.float16)
-    dv = torch.empty_like(v, dtype=torch.float16)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
     _ext.backward_into(q, k, v, grad_o, o, lse, causal, torch.float32, dq32, dk, dv)
     return dq32.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
 
@@ -61,7 +62,7 @@ class _FlashAttnBNHD(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, full_precision):
         B, H, N, D = q.shape
-        out = torch.empty((B, N, H, D), device=q.device, dtype=torch.float16)
+        out = torch.empty((B, N, H, D), device=q.device, dtype=q.dtype)
         o, lse = _ext.forward(q, k, v, causal, full_precision, o=out.transpose(1, 2))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal = causal
@@ -80,7 +81,7 @@ def flash_attn_bnhd(q, k, v, causal=False, full_precision=False):
 
 
 def flash_attn(q, k, v, causal=False, full_precision=False):
-    """Attention over fp16 CUDA tensors (fa_p100.py:48-55).
+    """Attention over fp16 (or bf16) CUDA tensors (fa_p100.py:48-55).
 
     q is (B, Hq, N, D); k and v are (B, Hkv, N, D) with Hq a multiple of Hkv.
     Hkv == Hq is ordinary multi-head; Hkv == 1 is multi-query; anything between

@@ -28,10 +28,19 @@ def _check_in(t, name):
     # fa_p100_ext.cu:31-35
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor")
-    if t.dtype != torch.float16:
-        raise RuntimeError(f"{name} must be fp16")
+    if t.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(f"{name} must be fp16 (or bf16)")
     if t.dim() != 4:
         raise RuntimeError(f"{name} must be (B, H, N, D)")
+
+
+def _dtype_code(q, *others):
+    """FA_B200_DTYPE_* of q; every other 16-bit tensor of the call must match."""
+    for t in others:
+        if t.dtype != q.dtype:
+            raise RuntimeError(f"all of q, k, v, dO and o must share one dtype; got {q.dtype} "
+                               f"and {t.dtype}")
+    return _lib.DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.DTYPE_FP16
 
 
 def _stream_ptr(device):
@@ -80,31 +89,33 @@ def _out(t, shape, dtype, device, name):
 
 
 def forward(q, k, v, causal, full_precision=False, o=None):
-    """O (B,Hq,N,D) fp16 and LSE (B,Hq,N) fp32 (natural log). fa_p100_ext.cu:53-83.
-    `o` may supply the output in any layout with a contiguous D axis."""
+    """O (B,Hq,N,D) in q's dtype and LSE (B,Hq,N) fp32 (natural log).
+    fa_p100_ext.cu:53-83. q, k, v are fp16 (the reference's type) or bf16; `o`
+    may supply the output in any layout with a contiguous D axis."""
     _check_in(q, "q")
     _check_in(k, "k")
     _check_in(v, "v")
+    dtype = _dtype_code(q, k, v)
     B, H, Hkv, N, D = _shapes(q, k, v)
     (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
-    o, so = _out(o, (B, H, N, D), torch.float16, q.device, "o")
+    o, so = _out(o, (B, H, N, D), q.dtype, q.device, "o")
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
         st = _lib.lib().fa_b200_forward_strided(
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, o.data_ptr(), so,
-            lse.data_ptr(), B, H, Hkv, N, D, 1 if causal else 0, 1 if full_precision else 0,
-            _stream_ptr(q.device))
+            lse.data_ptr(), B, H, Hkv, N, D, dtype, 1 if causal else 0,
+            1 if full_precision else 0, _stream_ptr(q.device))
     _lib.check(st, "fa_b200_forward_strided")
     return [o, lse]
 
 
 def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, dk=None,
                   dv=None):
-    """dq (dq_dtype), dk, dv. fp32 dq (the default, and `backward`) runs the
-    fused one-pass backward, whose dq adds are not bitwise deterministic; fp16
-    dq runs the two-kernel backward (dK/dV, then dQ), which is. dq, dk, dv may
-    be supplied in any layout with a contiguous D axis (new ones are
-    contiguous)."""
+    """dq (dq_dtype), dk, dv (q's dtype). fp32 dq (the default, and `backward`)
+    runs the fused one-pass backward, whose dq adds are not bitwise
+    deterministic; a 16-bit dq (q's dtype) runs the two-kernel backward (dK/dV,
+    then dQ), which is. dq, dk, dv may be supplied in any layout with a
+    contiguous D axis (new ones are contiguous)."""
     _check_in(q, "q")
     _check_in(dO, "dO")
     # fa_p100_ext.cu:106-115 checks only q and dO; k, v, o and lse are checked
@@ -116,14 +127,15 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, 
     B, H, Hkv, N, D = _shapes(q, k, v)
     if dO.shape != q.shape or o.shape != q.shape or lse.shape != (B, H, N):
         raise RuntimeError("dO and o must match q, and lse must be (B, Hq, N)")
-    if dq_dtype not in (torch.float32, torch.float16):
-        raise RuntimeError("dq_dtype must be float32 or float16")
+    dtype = _dtype_code(q, k, v, dO, o)
+    if dq_dtype not in (torch.float32, q.dtype):
+        raise RuntimeError(f"dq_dtype must be float32 or {q.dtype}")
     (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
     (dO, sdo), (o, so) = _layout(dO), _layout(o)
     lse = lse.contiguous()
     dq, sdq = _out(dq, (B, H, N, D), dq_dtype, q.device, "dq")
-    dk, sdk = _out(dk, (B, Hkv, N, D), torch.float16, q.device, "dk")
-    dv, sdv = _out(dv, (B, Hkv, N, D), torch.float16, q.device, "dv")
+    dk, sdk = _out(dk, (B, Hkv, N, D), q.dtype, q.device, "dk")
+    dv, sdv = _out(dv, (B, Hkv, N, D), q.dtype, q.device, "dv")
     lib = _lib.lib()
     ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
     ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
@@ -132,14 +144,14 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, 
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, dO.data_ptr(), sdo,
             o.data_ptr(), so, lse.data_ptr(), dq.data_ptr(), sdq,
             1 if dq_dtype == torch.float32 else 0, dk.data_ptr(), sdk, dv.data_ptr(), sdv,
-            ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, 1 if causal else 0, 0,
+            ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, dtype, 1 if causal else 0, 0,
             _stream_ptr(q.device))
     _lib.check(st, "fa_b200_backward_strided")
     return [dq, dk, dv]
 
 
 def backward(q, k, v, dO, o, lse, causal):
-    """dq fp32 (B,Hq,N,D), dk, dv fp16 (B,Hkv,N,D). fa_p100_ext.cu:103-142."""
+    """dq fp32 (B,Hq,N,D), dk, dv in q's dtype (B,Hkv,N,D). fa_p100_ext.cu:103-142."""
     return backward_into(q, k, v, dO, o, lse, causal, torch.float32)
 
 

@@ -14,7 +14,8 @@ Contract kept from the reference (fa_p100_hf.py:46-213):
     degrading: attention masks, output_attentions, head_mask, sliding windows,
     dropout, head_dim outside {64, 128}, a scale other than 1/sqrt(D), and
     q_len != kv_len (a populated KV cache);
-  * non-fp16 inputs are cast to fp16, silently under fp16 autocast and with a
+  * fp16 inputs run as they are, and so (beyond the reference) do bf16 ones;
+    other dtypes are cast to fp16, silently under fp16 autocast and with a
     single warning otherwise; the output is cast back to the input dtype.
 """
 import warnings
@@ -67,7 +68,11 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
         is_causal = bool(getattr(module, "is_causal", True)) and query.size(2) > 1
 
     in_dtype = query.dtype
-    if any(t.dtype != torch.float16 for t in (query, key, value)):
+    # fp16 (the reference's type) and bf16 run as they are; anything else
+    # (fp32, or a mix) is cast to fp16 as the reference does
+    native = all(t.dtype == torch.float16 for t in (query, key, value)) or all(
+        t.dtype == torch.bfloat16 for t in (query, key, value))
+    if not native:
         under_fp16_autocast = (torch.is_autocast_enabled("cuda")
                                and torch.get_autocast_dtype("cuda") == torch.float16)
         if not under_fp16_autocast and not _warned_cast:

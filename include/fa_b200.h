@@ -38,7 +38,16 @@ enum {
   FA_B200_ERR_WORKSPACE = 7,       /* workspace missing or smaller than required */
   FA_B200_ERR_DEVICE = 8,          /* current device is not compute capability 10.x */
   FA_B200_ERR_TOO_LARGE = 9,       /* a grid dimension would exceed CUDA limits */
-  FA_B200_ERR_SCRATCH_LIMIT = 10   /* B*Hq*roundup(N,128) above fa_b200_backward_noalloc_max_rows() */
+  FA_B200_ERR_SCRATCH_LIMIT = 10,  /* B*Hq*roundup(N,128) above fa_b200_backward_noalloc_max_rows() */
+  FA_B200_ERR_DTYPE = 11           /* dtype is not one of FA_B200_DTYPE_* */
+};
+
+/* Element type of the 16-bit tensors (q, k, v, o, dO, dk, dv, a 16-bit dq) of
+ * the strided entry points; the others take fp16, the reference's only type.
+ * Products are exact and accumulate in fp32 either way. */
+enum {
+  FA_B200_DTYPE_FP16 = 0,
+  FA_B200_DTYPE_BF16 = 1
 };
 
 /* Forward. Replaces fa_forward (reference fa_p100_ext.cu:53-83) and
@@ -57,15 +66,15 @@ typedef struct fa_b200_strides {
   int64_t batch, head, row;
 } fa_b200_strides;
 
-/* fa_b200_forward on tensors of any strided (B, H, N, D) layout with D
- * contiguous, e.g. (B, H, N, D) views of (B, N, H, D) storage as attention
+/* fa_b200_forward in fp16 or bf16 (`dtype`, FA_B200_DTYPE_*) on tensors of any
+ * strided (B, H, N, D) layout with D contiguous, e.g. (B, H, N, D) views of (B, N, H, D) storage as attention
  * layers produce them, so the caller needs no contiguous copies; o may be
  * strided too (lse stays (B, Hq, N) contiguous). The reference takes only
  * contiguous tensors and copies (fa_p100_ext.cu:56); no counterpart there. */
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
-                            float* lse, int B, int Hq, int Hkv, int N, int D, int causal,
-                            int full_precision, void* stream);
+                            float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
+                            int causal, int full_precision, void* stream);
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum
  * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the
@@ -111,7 +120,8 @@ int fa_b200_backward_stages(const void* q, const void* k, const void* v, const v
                             void* dv, void* workspace, size_t workspace_bytes, int B, int Hq,
                             int Hkv, int N, int D, int causal, int stages, void* stream);
 
-/* fa_b200_backward_stages on strided tensors (see fa_b200_strides): q, k, v,
+/* fa_b200_backward_stages in fp16 or bf16 (`dtype`) on strided tensors (see
+ * fa_b200_strides): q, k, v,
  * dO, o read and dq (fp32 or fp16), dk, dv written in their own layouts; lse
  * and the workspace are contiguous. stages == 0 selects the default for the dq
  * dtype. No counterpart in the reference (fa_p100_ext.cu:107-108 copies). */
@@ -121,7 +131,7 @@ int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, f
                              const float* lse, void* dq, fa_b200_strides sdq, int dq_fp32,
                              void* dk, fa_b200_strides sdk, void* dv, fa_b200_strides sdv,
                              void* workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
-                             int N, int D, int causal, int stages, void* stream);
+                             int N, int D, int dtype, int causal, int stages, void* stream);
 
 /* Backward that allocates nothing and takes no workspace. No counterpart in
  * the reference. For callers that cannot hand the library device memory of

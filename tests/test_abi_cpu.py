@@ -101,11 +101,11 @@ def S(b=4 * 16 * 64, h=16 * 64, n=64):
     return _lib.Strides(b, h, n)
 
 
-def fwd_strided(sq=None, so=None, o=P, D=64):
+def fwd_strided(sq=None, so=None, o=P, D=64, dtype=0):
     lib = _lib.lib()
     sq = sq or S()
     return lib.fa_b200_forward_strided(P, sq, P, S(2 * 16 * 64), P, S(2 * 16 * 64), o, so or S(),
-                                       P, 1, 4, 2, 16, D, 1, 0, None)
+                                       P, 1, 4, 2, 16, D, dtype, 1, 0, None)
 
 
 def test_strided_forward_argument_errors():
@@ -115,14 +115,16 @@ def test_strided_forward_argument_errors():
     assert fwd_strided(so=S(b=4 * 16 * 64 + 4)) == 4
     assert fwd_strided(o=MISALIGNED) == 4
     assert fwd_strided(D=96) == 2
+    assert fwd_strided(dtype=2) == 11      # FA_B200_ERR_DTYPE
+    assert fwd_strided(dtype=-1) == 11
 
 
-def bwd_strided(sdq=None, dq_fp32=1, stages=0, **kw):
+def bwd_strided(sdq=None, dq_fp32=1, stages=0, dtype=0):
     lib = _lib.lib()
     sq, skv = S(), S(2 * 16 * 64)
     return lib.fa_b200_backward_strided(
         P, sq, P, skv, P, skv, P, sq, P, sq, P, P, sdq or S(), dq_fp32, P, skv, P, skv,
-        P, 1 << 20, 1, 4, 2, 16, 64, 1, stages, None)
+        P, 1 << 20, 1, 4, 2, 16, 64, dtype, 1, stages, None)
 
 
 def test_strided_backward_argument_errors():
@@ -131,6 +133,7 @@ def test_strided_backward_argument_errors():
     assert bwd_strided(sdq=S(n=68), dq_fp32=0) == 4
     assert bwd_strided(stages=8, dq_fp32=0) == 3     # the fused stage needs an fp32 dq
     assert bwd_strided(stages=64) == 3
+    assert bwd_strided(dtype=7) == 11
 
 
 def test_strides_of_layouts():
