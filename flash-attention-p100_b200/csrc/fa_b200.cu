@@ -49,6 +49,7 @@ struct DeviceState {
   bool ready = false;
   int status = FA_B200_OK;
   int* err = nullptr;  // address of g_device_error on this device
+  int sms = 148;       // multiprocessors
 };
 
 std::mutex g_mu;
@@ -88,7 +89,7 @@ void set_smem_all() {
 
 // One-time, per-device set-up with that device current: architecture check,
 // opt-in to large dynamic shared memory, and the error word's address.
-int device_setup(int* dev_out, int** err_out) {
+int device_setup(int* dev_out, int** err_out, int* sms_out = nullptr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA_B200_ERR_DEVICE;
   // Bind the device's primary context to this host thread. The tensor-map
@@ -101,6 +102,7 @@ int device_setup(int* dev_out, int** err_out) {
   if (!st.ready) {
     int major = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
     if (major != 10) {
       st.status = FA_B200_ERR_DEVICE;
     } else {
@@ -125,6 +127,7 @@ int device_setup(int* dev_out, int** err_out) {
     st.ready = true;
   }
   *err_out = st.err;
+  if (sms_out) *sms_out = st.sms;
   return st.status;
 }
 
@@ -264,9 +267,9 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
 
 template <int D, bool BF>
 int launch_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,
-                    const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* ws, int B,
-                    int Hq, int Hkv, int N, int causal, int stages, const BwdLayout& L,
-                    cudaStream_t stream, int* err) {
+                    const float* lse, void* dq, int dq_fp32, void* dk, void* dv, float* ws,
+                    size_t ws_bytes, int B, int Hq, int Hkv, int N, int causal, int stages,
+                    const BwdLayout& L, int sms, cudaStream_t stream, int* err) {
   const uint64_t BH = static_cast<uint64_t>(B) * Hq, BHkv = static_cast<uint64_t>(B) * Hkv;
   const int nq128 = (N + 127) / 128;
   if (nq128 > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
@@ -301,6 +304,11 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   p.group = Hq / Hkv;
   p.causal = causal ? 1 : 0;
   p.dq_fp32 = dq_fp32 ? 1 : 0;
+  p.head_group = 1;
+  p.gsplit = 1;
+  p.gper = p.group;
+  p.n_batch = B;
+  p.dkv_acc = nullptr;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
 
@@ -329,10 +337,37 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const uint64_t hg_max = std::max<uint64_t>(1, (64ull << 20) / slice_bytes);
     const uint64_t n_groups = (BHkv + hg_max - 1) / hg_max;
     p.head_group = static_cast<int>((BHkv + n_groups - 1) / n_groups);
-    if (BHkv * static_cast<uint64_t>(nq128) > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-    bwd_fused_kernel<D, BF><<<static_cast<unsigned>(BHkv * nq128), FusedCfg<D>::THREADS,
-                          FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
+    if (BHkv * static_cast<uint64_t>(nq128) * 16 > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
+    // Too few (batch, kv-head) x key-block CTAs to fill the GPU and a GQA
+    // group to divide: split each group over several CTAs, which add their
+    // partial dK/dV into an fp32 accumulator in the workspace (when the caller
+    // sized it with fa_b200_backward_workspace_bytes_gqa).
+    const uint64_t units = BHkv * static_cast<uint64_t>(nq128);
+    const size_t rows_bytes = 2 * sizeof(float) * static_cast<size_t>(rows_pad);
+    const size_t acc_bytes = 2 * sizeof(float) * static_cast<size_t>(BHkv) * N * D;
+    if (p.group > 1 && units < 2ull * sms && ws_bytes >= rows_bytes + acc_bytes) {
+      const int want = std::min<int>(p.group, static_cast<int>((2ull * sms + units - 1) / units));
+      p.gper = (p.group + want - 1) / want;
+      p.gsplit = (p.group + p.gper - 1) / p.gper;
+    }
+    CUtensorMap tdkv = tdq;   // unused unless the group is split
+    if (p.gsplit > 1) {
+      p.dkv_acc = ws + 2 * rows_pad;
+      if (cudaMemsetAsync(p.dkv_acc, 0, acc_bytes, stream) != cudaSuccess)
+        return launch_status("the dK/dV accumulator memset");
+      if (!make_map4(&tdkv, p.dkv_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv, 2ull * B,
+                     contiguous(Hkv, N, D), 32))
+        return FA_B200_ERR_TENSOR_MAP;
+    }
+    bwd_fused_kernel<D, BF><<<static_cast<unsigned>(units * p.gsplit), FusedCfg<D>::THREADS,
+                              FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdkv, p);
     if (int st = launch_status("bwd_fused_kernel")) return st;
+    if (p.gsplit > 1) {
+      const long long total = 2ll * BHkv * N * (D / 8);
+      bwd_dkv_convert_kernel<BF><<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+          p.dkv_acc, p.dk, L.dk, p.dv, L.dv, B, Hkv, N, D, total);
+      if (int st = launch_status("bwd_dkv_convert_kernel")) return st;
+    }
   }
   if (stages & FA_B200_STAGE_DQ) {
     bwd_dq_kernel<D, BF><<<dim3(static_cast<unsigned>(BH), nq128), DqCfg<D>::THREADS, DqCfg<D>::SMEM,
@@ -511,17 +546,18 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
       !strides_ok(L.v, 2) || !strides_ok(L.dO, 2) || !strides_ok(L.o, 2) ||
       !strides_ok(L.dq, dq_fp32 ? 4 : 2) || !strides_ok(L.dk, 2) || !strides_ok(L.dv, 2))
     return FA_B200_ERR_ALIGNMENT;
-  int dev = 0;
+  int dev = 0, sms = 0;
   int* err = nullptr;
-  st = device_setup(&dev, &err);
+  st = device_setup(&dev, &err, &sms);
   if (st != FA_B200_OK) return st;
   float* ws = noalloc ? noalloc_scratch(dev) : static_cast<float*>(workspace);
+  const size_t ws_bytes = noalloc ? 0 : workspace_bytes;
   if (!ws) return FA_B200_ERR_DEVICE;
   auto s = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == FA_B200_DTYPE_BF16;
-#define FAB_BWD(DD, BB)                                                                     \
-  launch_backward<DD, BB>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, B, Hq, Hkv, N, causal, \
-                          stages, L, s, err)
+#define FAB_BWD(DD, BB)                                                                  \
+  launch_backward<DD, BB>(q, k, v, dO, o, lse, dq, dq_fp32, dk, dv, ws, ws_bytes, B, Hq, Hkv, N, \
+                          causal, stages, L, sms, s, err)
   if (D == 64) return bf ? FAB_BWD(64, true) : FAB_BWD(64, false);
   return bf ? FAB_BWD(128, true) : FAB_BWD(128, false);
 #undef FAB_BWD
@@ -564,6 +600,13 @@ size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {
   // Dv and LSE*log2e for every query row, each head padded to a multiple of
   // 128 rows (a multiple of 512 bytes, so the total needs no rounding).
   return 2 * static_cast<size_t>(B) * Hq * fab::pad_rows(N) * sizeof(float);
+}
+
+size_t fa_b200_backward_workspace_bytes_gqa(int B, int Hq, int Hkv, int N, int D) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || N < 1 || D < 1) return 0;
+  // the row values, then fp32 dK and dV accumulators for a split GQA group
+  return fa_b200_backward_workspace_bytes(B, Hq, N) +
+         2 * static_cast<size_t>(B) * Hkv * N * D * sizeof(float);
 }
 
 int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,

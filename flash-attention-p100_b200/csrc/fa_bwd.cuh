@@ -48,6 +48,9 @@ struct BwdParams {
   int n, n_pad, hq, group, causal;
   int dq_fp32;
   int head_group;      // fused kernel: (batch, kv-head) slices scheduled together
+  int gsplit, gper;    // fused kernel: GQA group split over gsplit CTAs of gper heads
+  int n_batch;         // B
+  float* dkv_acc;      // gsplit > 1: fp32 dK then dV, (2B, Hkv, N, D), added into
   float scale;         // 1/sqrt(D)
   float scale_log2;    // scale * log2(e)
 };
@@ -926,7 +929,8 @@ template <int D, bool BF>
 __global__ void __launch_bounds__(512, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
+                     const __grid_constant__ CUtensorMap tm_dq,
+                     const __grid_constant__ CUtensorMap tm_dkv, const BwdParams p) {
   using C = FusedCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (!smem_aligned_or_report(smem_raw, p.err)) return;
@@ -947,24 +951,30 @@ __global__ void __launch_bounds__(512, 1)
   // then block 1, and so on. CTAs that run together start at neighbouring query
   // blocks of the group's slices and advance in step, so the tiles they share
   // and the dQ rows they add into are L2 hits rather than DRAM round trips.
+  // With p.gsplit > 1 the heads of one GQA group are split over gsplit
+  // consecutive CTAs (gper heads each), which add their dK/dV into fp32.
   const int nkb = (p.n + C::BN - 1) / C::BN;
   const int hkv = p.hq / p.group;
+  const int split = static_cast<int>(blockIdx.x) % p.gsplit;
+  const int unit = static_cast<int>(blockIdx.x) / p.gsplit;
   int bkv, kvb;
   {
     const int per_group = p.head_group * nkb;
-    const int g0 = static_cast<int>(blockIdx.x) / per_group;
-    const int r = static_cast<int>(blockIdx.x) - g0 * per_group;
-    const int n_bkv = (gridDim.x / nkb);                 // B * Hkv
+    const int g0 = unit / per_group;
+    const int r = unit - g0 * per_group;
+    const int n_bkv = gridDim.x / (nkb * p.gsplit);     // B * Hkv
     const int hg = min(p.head_group, n_bkv - g0 * p.head_group);
     kvb = r / hg;
     bkv = g0 * p.head_group + r % hg;
   }
+  const int gh0 = split * p.gper;                       // this CTA's first head of the group
+  const int gcount = min(p.gper, p.group - gh0);
   const int b = bkv / hkv, kvh = bkv % hkv;
   const int kv0 = kvb * C::BN;
   const int nqb = (p.n + C::BM - 1) / C::BM;
   const int i_start = p.causal ? kvb : 0;   // BM == BN: the diagonal block
   const int nq_head = nqb - i_start;
-  const int total = p.group * nq_head;      // (group head, query block) steps
+  const int total = gcount * nq_head;       // (group head, query block) steps
   const Ctl ctl{abort_flag, p.err};
   auto slot_of = [](int it) { return it % C::STAGES; };
   auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
@@ -1012,7 +1022,7 @@ __global__ void __launch_bounds__(512, 1)
       constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
       auto prefetch_step = [&](int st) {
         const int q0p = (i_start + st % nq_head) * C::BM;
-        const int hqp = kvh * p.group + st / nq_head;
+        const int hqp = kvh * p.group + gh0 + st / nq_head;
         for (int c = 0; c < C::CH; ++c) {
           tma_prefetch_l2_4d(&tm_q, c * 64, q0p, hqp, b);
           tma_prefetch_l2_4d(&tm_do, c * 64, q0p, hqp, b);
@@ -1020,7 +1030,7 @@ __global__ void __launch_bounds__(512, 1)
       };
       for (int st = 0; st < kAhead && st < total; ++st) prefetch_step(st);
       for (int step = 0; step < total && ok; ++step) {
-        const int g = step / nq_head;
+        const int g = gh0 + step / nq_head;
         const int q0 = (i_start + step % nq_head) * C::BM;
         const int hq_g = kvh * p.group + g;
         const int bh = b * p.hq + hq_g;
@@ -1156,7 +1166,7 @@ __global__ void __launch_bounds__(512, 1)
     bool ok = true;
     for (int i = 0; i < total && ok; ++i) {
       const int qb0 = (i_start + i % nq_head) * C::BM;
-      const int bh = b * p.hq + kvh * p.group + i / nq_head;
+      const int bh = b * p.hq + kvh * p.group + gh0 + i / nq_head;
       ok = mbar_wait(b_dqfull, i & 1, ctl, kErrTimeoutEpilogue);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -1307,14 +1317,49 @@ __global__ void __launch_bounds__(512, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
+        if (p.gsplit == 1) {
 #pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          const int col = w * (D / 2) + 32 * c;
-          uint32_t v[32];
-          tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-          if (kvrow < p.n) store_row32_h<BF>(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
-          tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-          if (kvrow < p.n) store_row32_h<BF>(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
+          for (int c = 0; c < D / 64; ++c) {
+            const int col = w * (D / 2) + 32 * c;
+            uint32_t v[32];
+            tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
+            if (kvrow < p.n) store_row32_h<BF>(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
+            tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
+            if (kvrow < p.n) store_row32_h<BF>(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
+          }
+        } else {
+          // partial dK/dV of this split: 32-row x 32-column fp32 boxes staged in
+          // the ring and dS tile (idle now: every load and MMA has completed;
+          // the read-out warps' staging buffers lie beyond them) and added into
+          // the fp32 accumulator, dK as batch b and dV as batch B + b
+          constexpr int NB = D / 64;               // boxes per tensor per warp
+          const uint32_t wbox = s_ring + warp * (2 * NB * 4096);
+          const int krow0 = kv0 + 32 * (warp & 3);
+#pragma unroll 1
+          for (int t = 0; t < 2; ++t) {
+#pragma unroll 1
+            for (int c = 0; c < NB; ++c) {
+              uint32_t v[32];
+              tmem_ld32_sync(tmem + (t ? C::COL_DV : C::COL_DK) + w * (D / 2) + 32 * c + lane_off, v);
+              const uint32_t box = wbox + (t * NB + c) * 4096;
+#pragma unroll
+              for (int c4 = 0; c4 < 8; ++c4)
+                st_shared_v4(box + lane * 128 + ((c4 ^ (lane & 7)) << 4), v[4 * c4], v[4 * c4 + 1],
+                             v[4 * c4 + 2], v[4 * c4 + 3]);
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0 && krow0 < p.n) {
+#pragma unroll 1
+            for (int t = 0; t < 2; ++t)
+#pragma unroll 1
+              for (int c = 0; c < NB; ++c)
+                tma_reduce_add_4d(&tm_dkv, wbox + (t * NB + c) * 4096, w * (D / 2) + 32 * c, krow0,
+                                  kvh, t * (p.n_batch) + b);
+            bulk_commit_group();
+            bulk_wait_all();
+          }
         }
       }
     }
@@ -1327,6 +1372,40 @@ __global__ void __launch_bounds__(512, 1)
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+}  // namespace fab
+
+namespace fab {
+
+// The split fused backward's fp32 dK/dV accumulator -- (2B, Hkv, N, D), dK in
+// batches 0..B-1 and dV in B..2B-1 -- rounded to the 16-bit dk, dv (fp16, or bf16
+// when BF) in their own layouts. HBM-bound: one 32-byte read and one 16-byte
+// write per thread.
+template <bool BF>
+__global__ void __launch_bounds__(256) bwd_dkv_convert_kernel(const float* __restrict__ acc,
+                                                               uint16_t* __restrict__ dk, Strides sdk,
+                                                               uint16_t* __restrict__ dv, Strides sdv,
+                                                               int B, int hkv, int n, int d,
+                                                               long long total) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int per_row = d / 8;
+  const long long row = i / per_row;
+  const int part = static_cast<int>(i - row * per_row);
+  const int r = static_cast<int>(row % n);
+  const long long bh = row / n;                    // over (2B, Hkv)
+  const int h = static_cast<int>(bh % hkv);
+  const int bb = static_cast<int>(bh / hkv);
+  const float4* src = reinterpret_cast<const float4*>(acc + row * d) + 2 * part;
+  const float4 a = src[0], c = src[1];
+  uint4 pk;
+  pk.x = pack2<BF>(a.x, a.y);
+  pk.y = pack2<BF>(a.z, a.w);
+  pk.z = pack2<BF>(c.x, c.y);
+  pk.w = pack2<BF>(c.z, c.w);
+  uint16_t* dst = bb < B ? dk + sdk.at(bb, h, r) : dv + sdv.at(bb - B, h, r);
+  reinterpret_cast<uint4*>(dst)[part] = pk;
 }
 
 }  // namespace fab

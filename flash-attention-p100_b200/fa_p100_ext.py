@@ -137,7 +137,7 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, 
     dk, sdk = _out(dk, (B, Hkv, N, D), q.dtype, q.device, "dk")
     dv, sdv = _out(dv, (B, Hkv, N, D), q.dtype, q.device, "dv")
     lib = _lib.lib()
-    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
+    ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, H, Hkv, N, D)
     ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
         st = lib.fa_b200_backward_strided(

@@ -82,6 +82,15 @@ int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa
  * roundup(N, 128) rows: 2 * 4 * B * Hq * roundup(N, 128) bytes. */
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
 
+/* Workspace that also lets the fused backward split a GQA group over several
+ * CTAs when B * Hkv * ceil(N/128) is too small to fill the GPU (MQA, short
+ * sequences): fa_b200_backward_workspace_bytes(B, Hq, N) plus fp32 dK and dV
+ * accumulators, 2 * 4 * B * Hkv * N * D bytes. Any backward given at least
+ * this much may split; given less it does not. A split backward adds dK/dV
+ * partials in fp32 like dQ, so their last bits too depend on the add order. No counterpart in the
+ * reference, whose dK/dV are owned by one block each (flash_bwd.cuh:448-463). */
+size_t fa_b200_backward_workspace_bytes_gqa(int B, int Hq, int Hkv, int N, int D);
+
 /* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
  * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq, dk and dv (fp16).
  * dq_fp32 != 0 (dq fp32, as the reference returns it): stages ROWSUM | FUSED --

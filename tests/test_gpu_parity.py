@@ -103,8 +103,8 @@ def test_backward_op_contract(cuda, D, causal):
 @pytest.mark.parametrize("D,causal,Hq,Hkv,N", [(64, True, 4, 2, 333), (128, False, 8, 1, 700),
                                                (128, True, 4, 4, 1024)])
 def test_fused_stage_matches(cuda, D, causal, Hq, Hkv, N):
-    """The opt-in fused stage (dK, dV, dQ in one kernel, dQ by fp32 atomics)
-    against the oracle and the default kernels."""
+    """The fused stage requested explicitly (rows-only workspace, so no group
+    split) against the oracle and against the extension op."""
     import _lib
     import fa_p100_ext
     q, k, v, do = (t.to(cuda) for t in orc.seeded_inputs(1, Hq, Hkv, N, D, seed=8))
@@ -125,5 +125,37 @@ def test_fused_stage_matches(cuda, D, causal, Hq, Hkv, N):
     for got, ref in ((dq, rq), (dk, rk), (dv, rv)):
         assert orc.frob_rel(got, ref) < 1e-2
     dq2, dk2, dv2 = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
-    assert torch.equal(dk, dk2) and torch.equal(dv, dv2)
+    if Hq == Hkv:   # nothing to split: the same kernel, the same dK/dV bits
+        assert torch.equal(dk, dk2) and torch.equal(dv, dv2)
+    else:           # the op's workspace lets small GQA grids split (fp32 partial sums)
+        assert orc.frob_rel(dk, dk2) < 1e-3 and orc.frob_rel(dv, dv2) < 1e-3
     assert orc.frob_rel(dq, dq2) < 1e-4
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,D", [(2, 16, 1, 1537, 64), (1, 8, 2, 700, 128), (3, 6, 3, 260, 128)])
+def test_gqa_group_split_matches_unsplit(cuda, B, Hq, Hkv, N, D):
+    """With the larger workspace the fused backward splits small GQA/MQA grids
+    over several CTAs and adds partial dK/dV in fp32; with the rows-only
+    workspace it does not. Both must give the same gradients up to the order of
+    fp32 additions."""
+    import _lib
+    import fa_p100_ext
+    g = torch.Generator(device="cuda").manual_seed(11)
+    mk = lambda h: torch.randn(B, h, N, D, device="cuda", generator=g).half()
+    q, k, v, do = mk(Hq), mk(Hkv), mk(Hkv), mk(Hq)
+    o, lse = fa_p100_ext.forward(q, k, v, True)
+    split = fa_p100_ext.backward(q, k, v, do, o, lse, True)           # gqa-sized workspace
+    lib = _lib.lib()
+    dq = torch.empty(q.shape, device="cuda")
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, Hq, N)          # rows only: no split
+    ws = torch.empty(ws_bytes // 4, device="cuda")
+    st = lib.fa_b200_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                              o.data_ptr(), lse.data_ptr(), dq.data_ptr(), 1, dk.data_ptr(),
+                              dv.data_ptr(), ws.data_ptr(), ws_bytes, B, Hq, Hkv, N, D, 1,
+                              torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "fa_b200_backward")
+    for a, b in zip(split, (dq, dk, dv)):
+        a, b = a.float(), b.float()
+        assert (a - b).norm().item() <= 2e-3 * b.norm().item()
+    assert _lib.device_error(0) == 0

@@ -1,8 +1,8 @@
 """Strided layouts through the same kernels: q, k, v, dO, o as (B, H, N, D)
 views of (B, N, H, D) storage (what attention layers produce), and of rows
 padded inside a wider buffer, must give exactly the contiguous results -- the
-forward, dK/dV and the deterministic fp16 dQ bit for bit, the fp32 dQ (whose
-adds are unordered) to fp32 rounding. The layout-preserving autograd path used
+forward and the deterministic backward bit for bit, the fused backward (whose
+fp32 adds are unordered) to fp32 rounding. The layout-preserving autograd path used
 by the HF backend is checked against flash_attn."""
 import pytest
 import torch
@@ -59,13 +59,15 @@ def test_strided_matches_contiguous(cuda, case, layout):
                                       layout(torch.empty_like(v)))
     for a, b in zip(ref16, got16):
         assert torch.equal(a, b)
-    # fused backward (fp32 dq): dK/dV bit for bit, dQ to fp32 rounding
+    # fused backward (fp32 dq): dQ -- and dK/dV where a small GQA grid splits
+    # its group over CTAs that add fp32 partials -- to the order of fp32 adds
     ref = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
     got = fa_p100_ext.backward_into(qs, ks, vs, dos, os_, lse, causal, torch.float32,
                                     layout(torch.empty(q.shape, device="cuda")),
                                     layout(torch.empty_like(k)), layout(torch.empty_like(v)))
-    assert torch.equal(ref[1], got[1]) and torch.equal(ref[2], got[2])
-    assert (ref[0] - got[0]).abs().max().item() <= 1e-4 * ref[0].abs().max().item()
+    for a, b in zip(ref, got):
+        a, b = a.float(), b.float()
+        assert (a - b).norm().item() <= 1e-3 * a.norm().item()
 
 
 def test_bnhd_autograd_matches_flash_attn(cuda):
