@@ -231,9 +231,15 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ, STAGE_FUSED = 1, 2, 4, 8
 # The default backward for the reference's contract (fp32 dq): the row-sum
-# preprocess (which also zeroes dq) and the fused dK/dV/dQ kernel.
-KERNELS = ("fwd", "bwd_rowsum", "bwd_fused")
-STAGES = (STAGE_ROWSUM, STAGE_FUSED)
+# preprocess (which also zeroes dq) and the fused dK/dV/dQ kernel (plus, for a
+# GQA group split over CTAs, its dK/dV accumulator conversion). --deterministic
+# times the bitwise-reproducible backward instead: fp16 dq from the dK/dV and dQ
+# kernels.
+PATHS = {
+    "fused": (("fwd", "bwd_rowsum", "bwd_fused"), (STAGE_ROWSUM, STAGE_FUSED), 1),
+    "deterministic": (("fwd", "bwd_rowsum", "bwd_dkdv", "bwd_dq"),
+                      (STAGE_ROWSUM, STAGE_DKDV, STAGE_DQ), 0),
+}
 
 
 def kernel_work(name, B, Hq, Hkv, N, D, causal):
@@ -246,6 +252,10 @@ def kernel_work(name, B, Hq, Hkv, N, D, causal):
         return ff, "TFLOP/s", "tensor"
     if name == "bwd_fused":
         return 2.5 * ff, "TFLOP/s", "tensor"
+    if name == "bwd_dkdv":
+        return 2.0 * ff, "TFLOP/s", "tensor"
+    if name == "bwd_dq":
+        return 0.5 * ff, "TFLOP/s", "tensor"
     return 2.0 * B * Hq * N * D * 2 + 2 * B * Hq * N * 4 + B * Hq * N * D * 4, "GB/s", "hbm"
 
 
@@ -313,10 +323,11 @@ def run_ours(args, world, rank, local):
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
     o = torch.empty_like(q)
     lse = torch.empty(B, Hq, N, device=dev)
-    dq = torch.empty(q.shape, device=dev, dtype=torch.float32)
+    KERNELS, STAGES, dq_fp32 = PATHS["deterministic" if args.deterministic else "fused"]
+    dq = torch.empty(q.shape, device=dev, dtype=torch.float32 if dq_fp32 else torch.float16)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, Hq, N)
+    ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
     ws = torch.empty(ws_bytes // 4, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -327,7 +338,7 @@ def run_ours(args, world, rank, local):
     def bwd_stage(mask):
         return lib.fa_b200_backward_stages(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), o.data_ptr(),
-            lse.data_ptr(), dq.data_ptr(), 1, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
+            lse.data_ptr(), dq.data_ptr(), dq_fp32, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
             ws_bytes, B, Hq, Hkv, N, D, int(causal), mask, sp)
 
     def step(record):
@@ -362,7 +373,10 @@ def run_ours(args, world, rank, local):
             step(True)
         torch.cuda.synchronize(dev)
         barrier(world)
-    launches = len(KERNELS) * args.steps
+    # a GQA group split over CTAs adds the dK/dV accumulator conversion launch
+    split = (not args.deterministic and Hq > Hkv
+             and B * Hkv * ((N + 127) // 128) < 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+    launches = (len(KERNELS) + (1 if split else 0)) * args.steps
 
     per_kernel = {n: 0.0 for n in KERNELS}
     total_ms = 0.0
@@ -401,7 +415,7 @@ def run_ours(args, world, rank, local):
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
     barrier(world)
-    launches += 3 * args.steps   # forward, row-sum, fused backward
+    launches += (4 if split else 3) * args.steps   # forward, row-sum, fused backward (+ convert)
     e2e_ms = max_over_ranks(e2e_ms / args.steps, world, dev)
     del dq_d
     if _lib.device_error(local) != 0:
@@ -438,6 +452,8 @@ def run_ours(args, world, rank, local):
                    "causal": causal, "inputs": f"N(0,1)*{sc} fp16, seeded",
                    "l2": "flushed (256 MiB write) between steps, outside the timed events",
                    "parallelism": f"head-sharded x{world}" if world > 1 else "single GPU",
+                   "backward": ("deterministic (fp16 dq, dK/dV + dQ kernels)" if args.deterministic
+                                else "fused (fp32 dq, TMA reduce-adds)"),
                    "flops_per_step_per_gpu": step_flops,
                    "flop_convention": "fwd 4*B*Hq*D*pairs (causal pairs N(N+1)/2), fwd+bwd 3.5x"},
         "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
@@ -543,6 +559,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="C2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="time the bitwise-reproducible backward (fp16 dq, dK/dV + dQ kernels)")
     ap.add_argument("--ring", action="store_true",
                     help="ring context parallelism over the ranks (use with --workload C5)")
     ap.add_argument("--no-qwen3", action="store_true",
