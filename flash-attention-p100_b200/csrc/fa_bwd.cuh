@@ -1156,9 +1156,10 @@ __global__ void __launch_bounds__(512, 1)
     // Warp 8+q takes TMEM lanes 32q.. (query rows qb0+32q..) of dQ_i, all D
     // columns, frees the columns for dP^T_{i+1}, then stages its D/32 boxes of
     // 32 x 32 fp32 through two alternating 4 KiB buffers and adds each into dQ
-    // with a TMA reduce-add. Boxes are committed one bulk group each, buffers
-    // alternate, and a warp with no rows below N stages nothing, so the group
-    // that last read a buffer is always the second most recent one.
+    // with a TMA reduce-add. Before staging a box the warp waits until the TMA
+    // unit has read all its earlier boxes: each warp keeps at most one box in
+    // the queue that the Q/dO tile loads share (measured faster than letting
+    // both buffers fill), and a warp with no rows below N stages nothing.
     const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t stg = sbase + C::OFF_STG + (warp - 8) * 8192;
@@ -1186,7 +1187,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
       for (int h = 0; h < NB; ++h) {
         const uint32_t box = stg + (h & 1) * 4096;
-        if (lane == 0) bulk_wait_read_all_but_last();   // this buffer's last box has been read
+        if (lane == 0) bulk_wait_read_all();   // at most one box of this warp in the TMA queue
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < 8; ++c)
