@@ -11,7 +11,7 @@ The default workload is configs[1] (C2: B=1, Hq=Hkv=8, N=4096, D=128, causal).
 
 Our arm (--impl ours):
   value   whole-job TFLOPS with inputs resident in HBM, through the C ABI
-          (fa_b200_forward + fa_b200_backward_stages), L2 flushed (256 MiB
+          (fa_b200_forward_strided + fa_b200_backward_stages), L2 flushed (256 MiB
           write) between steps outside the timed events;
   e2e     the same metric through the public API (fa_p100.flash_attn + autograd
           backward) with q, k, v, dO copied from pinned host memory and dq, dk,
@@ -330,6 +330,12 @@ def run_ours(args, world, rank, local):
     ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
     ws = torch.empty(ws_bytes // 4, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    # the forward's workspace (a key-range split of its heaviest query blocks
+    # when the grid is small; none otherwise)
+    sq, skv = _lib.strides_of(q), _lib.strides_of(k)
+    fws_bytes = lib.fa_b200_forward_workspace_bytes(B, Hq, N, D, int(causal))
+    fws = torch.empty(max(fws_bytes // 4, 1), device=dev)
+    fws_ptr = fws.data_ptr() if fws_bytes else None
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     ev = {n: [] for n in KERNELS}
@@ -346,9 +352,10 @@ def run_ours(args, world, rank, local):
         marks = [torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] if record else None
         if record:
             marks[0].record(stream)
-        st = lib.fa_b200_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                                 lse.data_ptr(), B, Hq, Hkv, N, D, int(causal), 0, sp)
-        _lib.check(st, "fa_b200_forward")
+        st = lib.fa_b200_forward_strided(q.data_ptr(), sq, k.data_ptr(), skv, v.data_ptr(), skv,
+                                         o.data_ptr(), sq, lse.data_ptr(), B, Hq, Hkv, N, D,
+                                         _lib.DTYPE_FP16, int(causal), 0, fws_ptr, fws_bytes, sp)
+        _lib.check(st, "fa_b200_forward_strided")
         for i, mask in enumerate(STAGES):
             if record:
                 marks[i + 1].record(stream)

@@ -237,9 +237,25 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
   return FA_B200_OK;
 }
 
+// How many of each head's top m-blocks (256 query rows) the forward splits
+// into two key-range halves: none unless the (B*Hq, m-block) grid leaves SMs
+// idle; then all m-blocks whose two query tiles both have keys in both halves
+// (causal: every m-block but the first; else all, given two key blocks).
+int forward_split(int B, int Hq, int N, int causal, int sms) {
+  const long long mblocks = (N + 255) / 256;
+  if (static_cast<long long>(B) * Hq * mblocks >= sms) return 0;
+  if (causal) return static_cast<int>(mblocks - 1);
+  return (N + 127) / 128 >= 2 ? static_cast<int>(mblocks) : 0;
+}
+
+size_t forward_split_bytes(int B, int Hq, int D, int n_split) {
+  return 2 * static_cast<size_t>(B) * Hq * n_split * 256 * (D + 1) * sizeof(float);
+}
+
 template <int D, bool BF>
 int launch_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                   int Hkv, int N, int causal, const FwdLayout& L, cudaStream_t stream, int* err) {
+                   int Hkv, int N, int causal, const FwdLayout& L, void* ws, size_t ws_bytes,
+                   int sms, cudaStream_t stream, int* err) {
   using C = FwdCfg<D>;
   CUtensorMap tq, tk, tv;
   const uint64_t BH = static_cast<uint64_t>(B) * Hq;
@@ -259,10 +275,26 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
   p.causal = causal ? 1 : 0;
   p.n_mblocks = (N + 255) / 256;
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
-  if (p.n_mblocks > 65535 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-  dim3 grid(static_cast<unsigned>(BH), p.n_mblocks);
+  p.n_split = 0;
+  p.opart = p.lpart = nullptr;
+  if (p.n_mblocks > 32767 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
+  const int n_split = forward_split(B, Hq, N, causal, sms);
+  if (n_split > 0 && ws && ws_bytes >= forward_split_bytes(B, Hq, D, n_split)) {
+    p.n_split = n_split;
+    p.opart = static_cast<float*>(ws);
+    p.lpart = p.opart + 2 * BH * n_split * 256 * D;
+  }
+  dim3 grid(static_cast<unsigned>(BH), p.n_mblocks + p.n_split);
   fwd_kernel<D, BF><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
-  return launch_status("fwd_kernel");
+  if (int st = launch_status("fwd_kernel")) return st;
+  if (p.n_split > 0) {
+    const long long total = static_cast<long long>(BH) * p.n_split * 256 * (D / 8);
+    fwd_combine_kernel<D, BF><<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        p.opart, p.lpart, p.o, p.so, lse, N, Hq, p.n_mblocks, p.n_split,
+        static_cast<int>(BH), total);
+    return launch_status("fwd_combine_kernel");
+  }
+  return FA_B200_OK;
 }
 
 template <int D, bool BF>
@@ -492,25 +524,27 @@ namespace {
 Strides from_abi(fa_b200_strides st) { return Strides{st.batch, st.head, st.row}; }
 
 int forward_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                 int Hkv, int N, int D, int dtype, int causal, const FwdLayout& L, void* stream) {
+                 int Hkv, int N, int D, int dtype, int causal, const FwdLayout& L, void* ws,
+                 size_t ws_bytes, void* stream) {
   if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
   int st = check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
   if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(lse) ||
-      !strides_ok(L.q, 2) || !strides_ok(L.k, 2) || !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
+      (ws && !aligned16(ws)) || !strides_ok(L.q, 2) || !strides_ok(L.k, 2) ||
+      !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
     return FA_B200_ERR_ALIGNMENT;
-  int dev = 0;
+  int dev = 0, sms = 0;
   int* err = nullptr;
-  st = device_setup(&dev, &err);
+  st = device_setup(&dev, &err, &sms);
   if (st != FA_B200_OK) return st;
   auto s = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == FA_B200_DTYPE_BF16;
-  if (D == 64)
-    return bf ? launch_forward<64, true>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
-              : launch_forward<64, false>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
-  return bf ? launch_forward<128, true>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err)
-            : launch_forward<128, false>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, s, err);
+#define FAB_FWD(DD, BB) \
+  launch_forward<DD, BB>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, ws, ws_bytes, sms, s, err)
+  if (D == 64) return bf ? FAB_FWD(64, true) : FAB_FWD(64, false);
+  return bf ? FAB_FWD(128, true) : FAB_FWD(128, false);
+#undef FAB_FWD
 }
 
 // ws == nullptr: the built-in scratch of fa_b200_backward_noalloc.
@@ -581,18 +615,28 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
   (void)full_precision;
   const fab::Strides sq = fab::contiguous(Hq, N, D), skv = fab::contiguous(Hkv, N, D);
   return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, FA_B200_DTYPE_FP16, causal,
-                           fab::FwdLayout{sq, skv, skv, sq}, stream);
+                           fab::FwdLayout{sq, skv, skv, sq}, nullptr, 0, stream);
 }
 
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
                             float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
-                            int causal, int full_precision, void* stream) {
+                            int causal, int full_precision, void* workspace,
+                            size_t workspace_bytes, void* stream) {
   (void)full_precision;
   return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, dtype, causal,
                            fab::FwdLayout{fab::from_abi(sq), fab::from_abi(sk), fab::from_abi(sv),
                                           fab::from_abi(so)},
-                           stream);
+                           workspace, workspace_bytes, stream);
+}
+
+size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal) {
+  if (B < 1 || Hq < 1 || N < 1 || D < 1) return 0;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();   // a host without a device keeps the default
+  return fab::forward_split_bytes(B, Hq, D, fab::forward_split(B, Hq, N, causal, sms));
 }
 
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {

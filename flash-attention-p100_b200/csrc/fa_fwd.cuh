@@ -48,6 +48,14 @@ struct FwdParams {
   int causal;
   int n_mblocks;    // ceil(N / 256)
   float scale_log2; // softmax scale * log2(e)
+  // Key-range split for small grids: the n_split heaviest m-blocks of every
+  // head are done by two CTAs each (key blocks [0, half) and [half, end)),
+  // which write fp32 O (normalized by their own row sums) and LSE to opart /
+  // lpart, [part][B*Hq][n_split][256 rows] (x D for O); fwd_combine_kernel
+  // merges them.
+  int n_split;
+  float* opart;
+  float* lpart;
 };
 
 template <int D>
@@ -123,9 +131,13 @@ __global__ void __maxnreg__(96)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (B*Hq, m-blocks): every head's longest causal rows are dispatched first
+  // grid (B*Hq, m-blocks + split halves): every head's longest causal rows
+  // are dispatched first; y < 2*n_split are the two key-range halves of the
+  // n_split top m-blocks, the rest their unsplit m-blocks, top down
   const int bh = blockIdx.x;
-  const int mb = p.causal ? (p.n_mblocks - 1 - static_cast<int>(blockIdx.y)) : static_cast<int>(blockIdx.y);
+  const int y = static_cast<int>(blockIdx.y);
+  const int part = y < 2 * p.n_split ? (y & 1) : -1;
+  const int mb = p.n_mblocks - 1 - (part >= 0 ? y / 2 : y - p.n_split);
   const int m0 = mb * 256;
   // tensor-map coordinates: query head / batch, and the kv head it reads
   const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
@@ -135,6 +147,19 @@ __global__ void __maxnreg__(96)
   for (int t = 0; t < 2; ++t) {
     const int r0 = m0 + 128 * t;
     ntile[t] = (r0 >= p.n) ? 0 : (p.causal ? min(nblk, r0 / 128 + 1) : nblk);
+  }
+  // this CTA's key blocks [jb, je); ntile[] and nkv count from jb
+  int jb = 0;
+  {
+    const int full = max(ntile[0], ntile[1]);
+    int je = full;
+    if (part >= 0) {
+      const int half = full / 2;
+      jb = part ? half : 0;
+      je = part ? full : half;
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) ntile[t] = max(0, min(je, ntile[t]) - jb);
   }
   const int nkv = max(ntile[0], ntile[1]);
   const Ctl ctl{abort_flag, p.err};
@@ -178,14 +203,14 @@ __global__ void __maxnreg__(96)
       constexpr int kAhead = 2;  // L2 prefetch distance, in key blocks
       for (int j = 0; j < kAhead && j < nkv; ++j)
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_4d(&tm_k, c * 64, j * 128, hk_i, b_i);
-          tma_prefetch_l2_4d(&tm_v, c * 64, j * 128, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_k, c * 64, (jb + j) * 128, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_v, c * 64, (jb + j) * 128, hk_i, b_i);
         }
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + kAhead < nkv)
           for (int c = 0; c < C::CH; ++c) {
-            tma_prefetch_l2_4d(&tm_k, c * 64, (j + kAhead) * 128, hk_i, b_i);
-            tma_prefetch_l2_4d(&tm_v, c * 64, (j + kAhead) * 128, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_k, c * 64, (jb + j + kAhead) * 128, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_v, c * 64, (jb + j + kAhead) * 128, hk_i, b_i);
           }
 #pragma unroll 1
         for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
@@ -199,7 +224,7 @@ __global__ void __maxnreg__(96)
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
             tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
-                        c * 64, j * 128, hk_i, b_i);
+                        c * 64, (jb + j) * 128, hk_i, b_i);
         }
       }
       // Drain: do not leave the CTA while a load it issued may still land.
@@ -308,8 +333,9 @@ __global__ void __maxnreg__(96)
 #pragma unroll
         for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
       float* s = reinterpret_cast<float*>(&sr[0][0]);
-      const int col0 = j * 128 + c0;
-      const bool need_mask = (j * 128 + 128 > p.n) || (p.causal && j * 128 + 127 > m0 + 128 * t);
+      const int kb0 = (jb + j) * 128;   // this step's first key
+      const int col0 = kb0 + c0;
+      const bool need_mask = (kb0 + 128 > p.n) || (p.causal && kb0 + 127 > m0 + 128 * t);
       if (need_mask) {
         const int lim = p.causal ? min(p.n - 1, row) : (p.n - 1);
 #pragma unroll
@@ -400,6 +426,26 @@ __global__ void __maxnreg__(96)
         tc_fence_after();
         const float inv = 1.f / l;
         const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
+        if (part >= 0) {   // a key-range half: fp32 partial O and LSE for the combine
+          const size_t prow = ((static_cast<size_t>(part) * gridDim.x + bh) * p.n_split +
+                               (mb - (p.n_mblocks - p.n_split))) * 256 + 128 * t + r;
+          float* og = p.opart + prow * D + hf * (D / 2);
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t orow[32];
+            tmem_ld32(t_o + hf * (D / 2) + 32 * c, orow);
+            tmem_ld_wait(orow);
+            if (row < p.n) {
+#pragma unroll
+              for (int v = 0; v < 8; ++v)
+                reinterpret_cast<float4*>(og + 32 * c)[v] =
+                    make_float4(__uint_as_float(orow[4 * v]) * inv, __uint_as_float(orow[4 * v + 1]) * inv,
+                                __uint_as_float(orow[4 * v + 2]) * inv,
+                                __uint_as_float(orow[4 * v + 3]) * inv);
+            }
+          }
+          if (row < p.n && hf == 0) p.lpart[prow] = (m_used + __log2f(l)) * 0.69314718055994531f;
+        } else {
         uint16_t* orow_g = p.o + p.so.at(b_i, hq_i, row) + hf * (D / 2);
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
@@ -419,6 +465,7 @@ __global__ void __maxnreg__(96)
           }
         }
         if (row < p.n && hf == 0) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
+        }
       }
     }
   }
@@ -430,6 +477,49 @@ __global__ void __maxnreg__(96)
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+}  // namespace fab
+
+namespace fab {
+
+// Merges the two key-range halves of the split m-blocks: per row
+// LSE = log(e^LSE_0 + e^LSE_1) and O = O_0 e^(LSE_0 - LSE) + O_1 e^(LSE_1 - LSE),
+// written as the final 16-bit O (strides so) and LSE. One thread per 8 columns.
+template <int D, bool BF>
+__global__ void __launch_bounds__(256) fwd_combine_kernel(const float* __restrict__ opart,
+                                                          const float* __restrict__ lpart,
+                                                          uint16_t* __restrict__ o, Strides so,
+                                                          float* __restrict__ lse, int n, int hq,
+                                                          int n_mblocks, int n_split, int bhs,
+                                                          long long total) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  constexpr int PER_ROW = D / 8;
+  const long long prow = i / PER_ROW;                   // over (B*Hq, n_split, 256)
+  const int part8 = static_cast<int>(i - prow * PER_ROW);
+  const int lrow = static_cast<int>(prow % 256);
+  const long long bm = prow / 256;
+  const int ms = static_cast<int>(bm % n_split);
+  const int bh = static_cast<int>(bm / n_split);
+  const int row = (n_mblocks - n_split + ms) * 256 + lrow;
+  if (row >= n) return;
+  const long long half = static_cast<long long>(bhs) * n_split * 256;   // rows of one part
+  const float l0 = lpart[prow], l1 = lpart[half + prow];
+  const float m = fmaxf(l0, l1);
+  const float l = m + logf(expf(l0 - m) + expf(l1 - m));
+  const float w0 = expf(l0 - l), w1 = expf(l1 - l);
+  const float4* a = reinterpret_cast<const float4*>(opart + prow * D) + 2 * part8;
+  const float4* c = reinterpret_cast<const float4*>(opart + (half + prow) * D) + 2 * part8;
+  const float4 a0 = a[0], a1 = a[1], c0 = c[0], c1 = c[1];
+  uint4 pk;
+  pk.x = pack2<BF>(a0.x * w0 + c0.x * w1, a0.y * w0 + c0.y * w1);
+  pk.y = pack2<BF>(a0.z * w0 + c0.z * w1, a0.w * w0 + c0.w * w1);
+  pk.z = pack2<BF>(a1.x * w0 + c1.x * w1, a1.y * w0 + c1.y * w1);
+  pk.w = pack2<BF>(a1.z * w0 + c1.z * w1, a1.w * w0 + c1.w * w1);
+  const int b = bh / hq, h = bh % hq;
+  reinterpret_cast<uint4*>(o + so.at(b, h, row))[part8] = pk;
+  if (part8 == 0) lse[static_cast<size_t>(bh) * n + row] = l;
 }
 
 }  // namespace fab

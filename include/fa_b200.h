@@ -74,7 +74,17 @@ typedef struct fa_b200_strides {
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
                             float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
-                            int causal, int full_precision, void* stream);
+                            int causal, int full_precision, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* Workspace that lets fa_b200_forward_strided split the key range of its
+ * heaviest query blocks over two CTAs when B*Hq*ceil(N/256) blocks leave SMs
+ * of the current device idle (short sequences, few heads); 0 when it would not
+ * split. The halves' fp32 partial O and LSE are merged by a second kernel (by
+ * logaddexp, so the output matches the unsplit one to fp32 rounding). A
+ * forward given less workspace (or none: NULL, 0) does not split. No
+ * counterpart in the reference, one block per query tile (flash_fwd.cuh:127). */
+size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal);
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum
  * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the

@@ -105,7 +105,7 @@ def fwd_strided(sq=None, so=None, o=P, D=64, dtype=0):
     lib = _lib.lib()
     sq = sq or S()
     return lib.fa_b200_forward_strided(P, sq, P, S(2 * 16 * 64), P, S(2 * 16 * 64), o, so or S(),
-                                       P, 1, 4, 2, 16, D, dtype, 1, 0, None)
+                                       P, 1, 4, 2, 16, D, dtype, 1, 0, None, 0, None)
 
 
 def test_strided_forward_argument_errors():

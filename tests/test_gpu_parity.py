@@ -159,3 +159,30 @@ def test_gqa_group_split_matches_unsplit(cuda, B, Hq, Hkv, N, D):
         a, b = a.float(), b.float()
         assert (a - b).norm().item() <= 2e-3 * b.norm().item()
     assert _lib.device_error(0) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal", [(1, 8, 8, 4096, 128, True), (1, 4, 2, 1000, 64, True),
+                                                 (2, 2, 1, 777, 128, False), (1, 16, 16, 2048, 64, True)])
+def test_forward_key_split_matches_unsplit(cuda, B, Hq, Hkv, N, D, causal):
+    """On small grids the forward splits the key range of its heaviest query
+    blocks over two CTAs and merges the halves by their LSEs; without a
+    workspace it does not split. O and LSE must agree to rounding."""
+    import _lib
+    import fa_p100_ext
+    g = torch.Generator(device="cuda").manual_seed(21)
+    mk = lambda h: torch.randn(B, h, N, D, device="cuda", generator=g).half()
+    q, k, v = mk(Hq), mk(Hkv), mk(Hkv)
+    lib = _lib.lib()
+    assert lib.fa_b200_forward_workspace_bytes(B, Hq, N, D, int(causal)) > 0
+    o_split, lse_split = fa_p100_ext.forward(q, k, v, causal)         # with the workspace
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, N, device="cuda")
+    st = lib.fa_b200_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                             lse.data_ptr(), B, Hq, Hkv, N, D, int(causal), 0,
+                             torch.cuda.current_stream().cuda_stream)   # no workspace: unsplit
+    _lib.check(st, "fa_b200_forward")
+    assert (o_split.float() - o.float()).abs().max().item() <= 2e-3
+    assert (lse_split - lse).abs().max().item() <= 1e-4
+    rq = orc.attention(q, k, v, causal, device=cuda)
+    assert orc.rel(o_split, rq) < 6e-2
+    assert _lib.device_error(0) == 0
