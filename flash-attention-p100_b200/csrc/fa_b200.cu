@@ -285,7 +285,9 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
     p.lpart = p.opart + 2 * BH * n_split * 256 * D;
   }
   dim3 grid(static_cast<unsigned>(BH), p.n_mblocks + p.n_split);
-  fwd_kernel<D, BF><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, p);
+  CUtensorMap to;   // O output, 64-column x 128-row boxes
+  if (!make_map4(&to, o, dt, 2, D, N, Hq, B, L.o, 128)) return FA_B200_ERR_TENSOR_MAP;
+  fwd_kernel<D, BF><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, to, p);
   if (int st = launch_status("fwd_kernel")) return st;
   if (p.n_split > 0) {
     const long long total = static_cast<long long>(BH) * p.n_split * 256 * (D / 8);
@@ -391,8 +393,12 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
                      contiguous(Hkv, N, D), 32))
         return FA_B200_ERR_TENSOR_MAP;
     }
+    CUtensorMap tdk, tdv;   // dK / dV outputs, 64-column x 128-row boxes
+    if (!make_map4(&tdk, dk, dt, 2, D, N, Hkv, B, L.dk, 128) ||
+        !make_map4(&tdv, dv, dt, 2, D, N, Hkv, B, L.dv, 128))
+      return FA_B200_ERR_TENSOR_MAP;
     bwd_fused_kernel<D, BF><<<static_cast<unsigned>(units * p.gsplit), FusedCfg<D>::THREADS,
-                              FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdkv, p);
+                              FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdkv, tdk, tdv, p);
     if (int st = launch_status("bwd_fused_kernel")) return st;
     if (p.gsplit > 1) {
       const long long total = 2ll * BHkv * N * (D / 8);

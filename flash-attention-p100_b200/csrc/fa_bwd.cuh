@@ -874,8 +874,9 @@ namespace fab {
 // TMEM: S^T 0..127, with P^T (fp16 pairs) written back over cols 32..95 |
 //       dP^T 128..255, with dS^T (fp16 pairs) written back over cols 160..223,
 //       then (D = 128) dQ_i | dV 256.. | dK 256+D.. | (D = 64) dQ 384..
-// Shared: K, V, a 3-slot Q/dO ring, the dS tile [key][query], two 4 KiB dQ
-// staging boxes per read-out warp, LSE/Dv slices for two steps.
+// Shared: K, V, a 2-slot Q ring and a 1-slot (D = 64: 2-slot) dO ring, the dS
+// tile [key][query], two 4 KiB dQ staging boxes per read-out warp, LSE/Dv
+// slices for two steps.
 // MMA order per step i (brackets = what it waits for):
 //   [P_i] dV_i = P^T dO (A in TMEM) ; [Q_{i+1}] S^T_{i+1} ;
 //   [dS_i] dK_i = dS^T Q (A in TMEM), dQ_i = dS K (A = the dS tile read
@@ -889,16 +890,21 @@ namespace fab {
 // the compute threads read dP_i; dP^T_{i+1} after the read-out warps read
 // dQ_i). The dS
 // tile is rewritten for step i+1 only after dP^T_{i+1} completed, which was
-// issued after dK_i and dQ_i. The Q slot of step i is released after dK_i and
-// the producer fills the ring in order, so the LSE/Dv slice buffer i & 1 is
-// reloaded (for step i+2) only after every compute thread finished step i.
+// issued after dK_i and dQ_i. The Q slot of step i is released after dK_i,
+// so the LSE/Dv slice buffer i & 1, loaded with Q, is reloaded (for step i+2)
+// only after every compute thread finished step i; the dO slot of step i is
+// released after dV_i, which gives the load of dO_{i+1} the rest of step i.
 // ---------------------------------------------------------------------------
 template <int D>
 struct FusedCfg {
   static constexpr int BN = 128, BM = 128, CH = D / 64;
   static constexpr int TILE = 128 * D * 2;
-  static constexpr int STAGES = (D == 64) ? 4 : 3;   // 3 or 4 keep the slice buffers safe
-  static_assert(STAGES == 3 || STAGES == 4, "slice-buffer reuse assumes a 3- or 4-slot ring");
+  // Q and dO tiles live in two rings: QS slots for Q (a Q slot frees when
+  // dK_i has read it) and OS for dO (free once dV_i has read it, early in the
+  // step, so dO_{i+1} has most of a step to arrive before dP^T_{i+1})
+  static constexpr int STAGES = (D == 64) ? 4 : 3;
+  static constexpr int QS = 2, OS = STAGES - QS;
+  static_assert(QS == 2, "the LSE/Dv slice buffers are double-buffered with the Q ring");
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_RING = OFF_V + TILE;
@@ -906,8 +912,8 @@ struct FusedCfg {
   static constexpr int OFF_STG = OFF_DS + 32768;             // 4 warps x 2 x (32 rows x 32 fp32)
   static constexpr int OFF_LSE = OFF_STG + 8 * 4096;         // [2][128] LSE*log2e, [2][128] Dv*scale
   static constexpr int OFF_BAR = OFF_LSE + 2048;
-  // kv, full[ST], empty[ST], s, dp, p, ds, dqfull, dqfree, fin
-  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  // k, full[ST], empty[ST], s, dp, p, ds, dqfull, dqfree, fin, v
+  static constexpr int NBAR = 1 + 2 * STAGES + 8;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;     // window must start 1024-aligned
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 512;
@@ -930,7 +936,9 @@ __global__ void __launch_bounds__(512, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_dq,
-                     const __grid_constant__ CUtensorMap tm_dkv, const BwdParams p) {
+                     const __grid_constant__ CUtensorMap tm_dkv,
+                     const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                     const BwdParams p) {
   using C = FusedCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (!smem_aligned_or_report(smem_raw, p.err)) return;
@@ -940,7 +948,8 @@ __global__ void __launch_bounds__(512, 1)
   const uint32_t b_kv = sbase + C::OFF_BAR;
   const uint32_t b_full = b_kv + 8, b_empty = b_full + 8 * C::STAGES;
   const uint32_t b_s = b_empty + 8 * C::STAGES, b_dp = b_s + 8, b_p = b_dp + 8, b_ds = b_p + 8,
-                 b_dqfull = b_ds + 8, b_dqfree = b_dqfull + 8, b_fin = b_dqfree + 8;
+                 b_dqfull = b_ds + 8, b_dqfree = b_dqfull + 8, b_fin = b_dqfree + 8,
+                 b_v = b_fin + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -976,8 +985,11 @@ __global__ void __launch_bounds__(512, 1)
   const int nq_head = nqb - i_start;
   const int total = gcount * nq_head;       // (group head, query block) steps
   const Ctl ctl{abort_flag, p.err};
-  auto slot_of = [](int it) { return it % C::STAGES; };
-  auto ph_of = [](int it) { return static_cast<uint32_t>((it / C::STAGES) & 1); };
+  // Q_i in ring slot i % QS, dO_i in slot QS + i % OS; phase = use count & 1
+  auto q_slot = [](int i) { return i % C::QS; };
+  auto q_ph = [](int i) { return static_cast<uint32_t>((i / C::QS) & 1); };
+  auto o_slot = [](int i) { return C::QS + i % C::OS; };
+  auto o_ph = [](int i) { return static_cast<uint32_t>((i / C::OS) & 1); };
 
   if (threadIdx.x == 0) {
     mbar_init(b_kv, 1);
@@ -992,6 +1004,7 @@ __global__ void __launch_bounds__(512, 1)
     mbar_init(b_dqfull, 1);
     mbar_init(b_dqfree, C::NREADOUT);
     mbar_init(b_fin, 1);
+    mbar_init(b_v, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1011,13 +1024,12 @@ __global__ void __launch_bounds__(512, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(b_kv, 2 * C::TILE);
+      // K first and V after Q_0: S^T_0 needs K and Q_0, dP^T_0 V and dO_0
+      mbar_arrive_expect_tx(b_kv, C::TILE);
 #pragma unroll
-      for (int c = 0; c < C::CH; ++c) {
-        tma_load_4d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, kvh, b);
-        tma_load_4d(s_v + c * 16384, &tm_v, b_kv, c * 64, kv0, kvh, b);
-      }
-      int it = 0;
+      for (int c = 0; c < C::CH; ++c) tma_load_4d(s_k + c * 16384, &tm_k, b_kv, c * 64, kv0, kvh, b);
+      bool v_issued = false;
+      int nq = 0, ndo = 0;       // loads issued into the Q and the dO ring
       bool ok = true;
       constexpr int kAhead = 2;  // L2 prefetch distance, in query steps
       auto prefetch_step = [&](int st) {
@@ -1035,29 +1047,48 @@ __global__ void __launch_bounds__(512, 1)
         const int hq_g = kvh * p.group + g;
         const int bh = b * p.hq + hq_g;
         if (step + kAhead < total) prefetch_step(step + kAhead);
-#pragma unroll 1
-        for (int kind = 0; kind < 2; ++kind, ++it) {  // Q_i (+LSE, Dv) then dO_i
-          const int slot = slot_of(it);
-          ok = mbar_wait(b_empty + 8 * slot, ph_of(it) ^ 1, ctl, kErrTimeoutLoad);
+        // Q_step with its LSE and Dv slices: the slot frees when dK_{step-2}
+        // has read it, after every compute thread finished step-2, so the
+        // slice buffer step & 1 is free as well
+        {
+          const int slot = q_slot(step);
+          ok = mbar_wait(b_empty + 8 * slot, q_ph(step) ^ 1, ctl, kErrTimeoutLoad);
           if (!ok) break;
           const uint32_t fb = b_full + 8 * slot;
           const uint32_t dst = s_ring + slot * C::TILE;
-          mbar_arrive_expect_tx(fb, kind ? C::TILE : C::TILE + 1024);
+          mbar_arrive_expect_tx(fb, C::TILE + 1024);
 #pragma unroll
-          for (int c = 0; c < C::CH; ++c)
-            tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_do : (const void*)&tm_q, fb,
-                        c * 64, q0, hq_g, b);
-          if (!kind) {
-            const size_t off = static_cast<size_t>(bh) * p.n_pad + q0;
-            const uint32_t ls = s_lse + (step & 1) * 512;
-            bulk_load(ls, p.lse2 + off, 512, fb);
-            bulk_load(ls + 1024, p.dvec + off, 512, fb);
-          }
+          for (int c = 0; c < C::CH; ++c) tma_load_4d(dst + c * 16384, &tm_q, fb, c * 64, q0, hq_g, b);
+          const size_t off = static_cast<size_t>(bh) * p.n_pad + q0;
+          const uint32_t ls = s_lse + (step & 1) * 512;
+          bulk_load(ls, p.lse2 + off, 512, fb);
+          bulk_load(ls + 1024, p.dvec + off, 512, fb);
+          ++nq;
+        }
+        if (!v_issued) {
+          mbar_arrive_expect_tx(b_v, C::TILE);
+#pragma unroll
+          for (int c = 0; c < C::CH; ++c) tma_load_4d(s_v + c * 16384, &tm_v, b_v, c * 64, kv0, kvh, b);
+          v_issued = true;
+        }
+        // dO_step: the slot frees when dV_{step-OS} has read it
+        {
+          const int slot = o_slot(step);
+          ok = mbar_wait(b_empty + 8 * slot, o_ph(step) ^ 1, ctl, kErrTimeoutLoad);
+          if (!ok) break;
+          const uint32_t fb = b_full + 8 * slot;
+          const uint32_t dst = s_ring + slot * C::TILE;
+          mbar_arrive_expect_tx(fb, C::TILE);
+#pragma unroll
+          for (int c = 0; c < C::CH; ++c) tma_load_4d(dst + c * 16384, &tm_do, fb, c * 64, q0, hq_g, b);
+          ++ndo;
         }
       }
       if (!ok) {
         drain_loads(b_kv, 1, 1);
-        drain_loads(b_full, it, C::STAGES);
+        if (v_issued) drain_loads(b_v, 1, 1);
+        drain_loads(b_full, nq, C::QS);
+        drain_loads(b_full + 8 * C::QS, ndo, C::OS);
       }
     }
   } else if (warp == C::MMA_WARP) {
@@ -1075,43 +1106,43 @@ __global__ void __launch_bounds__(512, 1)
           mma_ss(d_tmem, sdesc_add(da, off), sdesc_add(db, off), id_t, kk > 0 ? 1u : 0u);
         }
       };
-      auto slot_addr = [&](int it) { return s_ring + slot_of(it) * C::TILE; };
+      auto slot_addr = [&](int slot) { return s_ring + slot * C::TILE; };
       const uint64_t d_dsm = sdesc_sw128(s_ds, 16384, 1024);    // dS tile as MN-major A
       const uint64_t d_kmn = sdesc_sw128(s_k, 16384, 1024);     // K as MN-major B
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
-      if (ok) ok = mbar_wait(b_full + 8 * slot_of(0), ph_of(0), ctl, kErrTimeoutMma);
+      if (ok) ok = mbar_wait(b_full + 8 * q_slot(0), q_ph(0), ctl, kErrTimeoutMma);
       if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_S, s_k, slot_addr(0));
+        issue_t(tmem + C::COL_S, s_k, slot_addr(q_slot(0)));
         mma_commit(b_s);
-        ok = mbar_wait(b_full + 8 * slot_of(1), ph_of(1), ctl, kErrTimeoutMma);
+        ok = mbar_wait(b_v, 0, ctl, kErrTimeoutMma) &&
+             mbar_wait(b_full + 8 * o_slot(0), o_ph(0), ctl, kErrTimeoutMma);
       }
       if (ok) {
         tc_fence_after();
-        issue_t(tmem + C::COL_DP, s_v, slot_addr(1));
+        issue_t(tmem + C::COL_DP, s_v, slot_addr(o_slot(0)));
         mma_commit(b_dp);
       }
       for (int i = 0; i < total && ok; ++i) {
-        const int it_q = 2 * i, it_do = 2 * i + 1;
         const bool more = i + 1 < total;
         // dV_i += P_i^T dO_i
         ok = mbar_wait(b_p, i & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
         {
-          const uint64_t ddo = sdesc_sw128(slot_addr(it_do), 16384, 1024);
+          const uint64_t ddo = sdesc_sw128(slot_addr(o_slot(i)), 16384, 1024);
 #pragma unroll
           for (int kk = 0; kk < C::BM / 16; ++kk)
             mma_ts(tmem + C::COL_DV, tmem + C::COL_P + kk * 8, sdesc_add(ddo, kk * 2048), id_g,
                    (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(b_empty + 8 * slot_of(it_do));
+        mma_commit(b_empty + 8 * o_slot(i));
         // S^T_{i+1}: its P phase overlaps dK_i and dQ_i
         if (more) {
-          ok = mbar_wait(b_full + 8 * slot_of(it_q + 2), ph_of(it_q + 2), ctl, kErrTimeoutMma);
+          ok = mbar_wait(b_full + 8 * q_slot(i + 1), q_ph(i + 1), ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_t(tmem + C::COL_S, s_k, slot_addr(it_q + 2));
+          issue_t(tmem + C::COL_S, s_k, slot_addr(q_slot(i + 1)));
           mma_commit(b_s);
         }
         // dK_i += dS_i^T Q_i ; dQ_i = dS_i K
@@ -1119,13 +1150,13 @@ __global__ void __launch_bounds__(512, 1)
         if (!ok) break;
         tc_fence_after();
         {
-          const uint64_t dq_mn = sdesc_sw128(slot_addr(it_q), 16384, 1024);
+          const uint64_t dq_mn = sdesc_sw128(slot_addr(q_slot(i)), 16384, 1024);
 #pragma unroll
           for (int kk = 0; kk < C::BM / 16; ++kk)
             mma_ts(tmem + C::COL_DK, tmem + C::COL_DS + kk * 8, sdesc_add(dq_mn, kk * 2048), id_g,
                    (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(b_empty + 8 * slot_of(it_q));
+        mma_commit(b_empty + 8 * q_slot(i));
         if (C::DQ_OWN_COLS && i > 0) {   // dQ_{i-1} has been read out of its columns
           ok = mbar_wait(b_dqfree, (i - 1) & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
@@ -1138,10 +1169,10 @@ __global__ void __launch_bounds__(512, 1)
         mma_commit(b_dqfull);
         if (more) {
           ok = (C::DQ_OWN_COLS || mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma)) &&
-               mbar_wait(b_full + 8 * slot_of(it_do + 2), ph_of(it_do + 2), ctl, kErrTimeoutMma);
+               mbar_wait(b_full + 8 * o_slot(i + 1), o_ph(i + 1), ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_t(tmem + C::COL_DP, s_v, slot_addr(it_do + 2));
+          issue_t(tmem + C::COL_DP, s_v, slot_addr(o_slot(i + 1)));
           mma_commit(b_dp);
         }
       }
@@ -1201,7 +1232,7 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
     }
-    if (lane == 0) bulk_wait_all();   // every dQ box added before the CTA exits
+    if (lane == 0) bulk_wait_read_all();   // the TMA unit has read every staged dQ box
   } else if (warp < 8) {
     regs_raise<C::REGS_COMPUTE>();
     // ------------------------------------------------------------ compute (warps 0-7)
@@ -1216,9 +1247,8 @@ __global__ void __launch_bounds__(512, 1)
     // P_i^T = exp2(S^T * scale*log2e - LSE*log2e), written over S^T in TMEM
     auto phase_p = [&](int i) -> bool {
       const int q0 = (i_start + i % nq_head) * C::BM + 64 * w;
-      const int it_q = 2 * i;
       const bool need_mask = (q0 + 64 > p.n) || (p.causal && q0 < kv0 + 127);
-      bool ok = mbar_wait(b_full + 8 * slot_of(it_q), ph_of(it_q), ctl, kErrTimeoutSoftmax) &&
+      bool ok = mbar_wait(b_full + 8 * q_slot(i), q_ph(i), ctl, kErrTimeoutSoftmax) &&
                 mbar_wait(b_s, i & 1, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) return false;
@@ -1319,15 +1349,21 @@ __global__ void __launch_bounds__(512, 1)
       if (ok) {
         tc_fence_after();
         if (p.gsplit == 1) {
+          // dV and dK rounded to 16 bits, staged as 64-column swizzled boxes in
+          // the idle Q/dO ring (every load and MMA has completed) and written
+          // by TMA stores: whole 128-byte rows instead of one row per thread
 #pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            const int col = w * (D / 2) + 32 * c;
-            uint32_t v[32];
-            tmem_ld32_sync(tmem + C::COL_DV + col + lane_off, v);
-            if (kvrow < p.n) store_row32_h<BF>(p.dv + p.sdv.at(b, kvh, kvrow) + col, v, 1.f);
-            tmem_ld32_sync(tmem + C::COL_DK + col + lane_off, v);
-            if (kvrow < p.n) store_row32_h<BF>(p.dk + p.sdk.at(b, kvh, kvrow) + col, v, 1.f);
-          }
+          for (int t = 0; t < 2; ++t)
+#pragma unroll 1
+            for (int c = 0; c < D / 64; ++c) {
+              const int col = w * (D / 2) + 32 * c;
+              uint32_t v[32];
+              tmem_ld32_sync(tmem + (t ? C::COL_DK : C::COL_DV) + col + lane_off, v);
+              float x[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) x[e] = __uint_as_float(v[e]);
+              st_row32_sw128<BF>(s_ring + t * C::TILE + (col / 64) * 16384, r, (col % 64) / 32, x);
+            }
         } else {
           // partial dK/dV of this split: 32-row x 32-column fp32 boxes staged in
           // the ring and dS tile (idle now: every load and MMA has completed;
@@ -1359,9 +1395,25 @@ __global__ void __launch_bounds__(512, 1)
                 tma_reduce_add_4d(&tm_dkv, wbox + (t * NB + c) * 4096, w * (D / 2) + 32 * c, krow0,
                                   kvh, t * (p.n_batch) + b);
             bulk_commit_group();
-            bulk_wait_all();
+            bulk_wait_read_all();   // boxes read: shared memory may be released
           }
         }
+      }
+    }
+    if (p.gsplit == 1) {
+      // every compute thread gets here once, whichever path it took above; a
+      // thread that skipped its staging raised the abort flag first
+      fence_async_smem();
+      named_bar_sync(1, C::NCOMPUTE);
+      if (threadIdx.x == 0 && total > 0 && *abort_flag == 0) {
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t)
+#pragma unroll 1
+          for (int c = 0; c < D / 64; ++c)
+            tma_store_4d(t ? (const void*)&tm_dk : (const void*)&tm_dv, s_ring + t * C::TILE + c * 16384,
+                         64 * c, kv0, kvh, b);
+        bulk_commit_group();
+        bulk_wait_read_all();   // boxes read: shared memory may be released
       }
     }
   }

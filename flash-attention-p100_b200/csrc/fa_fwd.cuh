@@ -114,7 +114,8 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
 template <int D, bool BF>
 __global__ void __maxnreg__(96)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+               const FwdParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -446,26 +447,41 @@ __global__ void __maxnreg__(96)
           }
           if (row < p.n && hf == 0) p.lpart[prow] = (m_used + __log2f(l)) * 0.69314718055994531f;
         } else {
-        uint16_t* orow_g = p.o + p.so.at(b_i, hq_i, row) + hf * (D / 2);
+        // O rows rounded to 16 bits, staged as 64-column swizzled boxes over
+        // this tile's Q (every MMA that reads Q_t has completed) and written
+        // by TMA stores below
+        const uint32_t s_qt = t ? s_q1 : s_q0;
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
+          const int col = hf * (D / 2) + 32 * c;
           uint32_t orow[32];
-          tmem_ld32(t_o + hf * (D / 2) + 32 * c, orow);
+          tmem_ld32(t_o + col, orow);
           tmem_ld_wait(orow);
-          if (row < p.n) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 pk;
-              pk.x = pack2<BF>(__uint_as_float(orow[8 * v + 0]) * inv, __uint_as_float(orow[8 * v + 1]) * inv);
-              pk.y = pack2<BF>(__uint_as_float(orow[8 * v + 2]) * inv, __uint_as_float(orow[8 * v + 3]) * inv);
-              pk.z = pack2<BF>(__uint_as_float(orow[8 * v + 4]) * inv, __uint_as_float(orow[8 * v + 5]) * inv);
-              pk.w = pack2<BF>(__uint_as_float(orow[8 * v + 6]) * inv, __uint_as_float(orow[8 * v + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow_g + 32 * c + 8 * v) = pk;
-            }
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int piece = 4 * ((col % 64) / 32) + q4;
+            st_shared_v4(s_qt + (col / 64) * 16384 + r * 128 + ((piece ^ (r & 7)) << 4),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 0]) * inv, __uint_as_float(orow[8 * q4 + 1]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 2]) * inv, __uint_as_float(orow[8 * q4 + 3]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 4]) * inv, __uint_as_float(orow[8 * q4 + 5]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 6]) * inv, __uint_as_float(orow[8 * q4 + 7]) * inv));
           }
         }
         if (row < p.n && hf == 0) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
         }
+      }
+    }
+    if (part < 0) {
+      // every thread of the tile gets here once, whichever path it took above;
+      // a thread that skipped its staging raised the abort flag first
+      fence_async_smem();
+      named_bar_sync(1 + t, 256);
+      if ((threadIdx.x & 255) == 0 && nt > 0 && *abort_flag == 0) {
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c)
+          tma_store_4d(&tm_o, (t ? s_q1 : s_q0) + c * 16384, 64 * c, m0 + 128 * t, hq_i, b_i);
+        bulk_commit_group();
+        bulk_wait_read_all();   // boxes read: shared memory may be released
       }
     }
   }

@@ -227,6 +227,16 @@ __device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t src
       "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
       : "memory");
 }
+// Tiled TMA store of one shared-memory box to global memory (bulk async group);
+// rows and columns outside the tensor are not written.
+__device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group"
+      " [%0, {%1, %2, %3, %4}], [%5];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
