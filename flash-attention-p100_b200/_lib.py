@@ -28,6 +28,7 @@ SIGNATURES = {
     "fa_b200_forward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P,
                                      _I, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "fa_b200_forward_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+    "fa_b200_merge_partial": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P,
                                       _P, _S, _I, _P, _S, _P, _S, _P, _SZ,
                                       _I, _I, _I, _I, _I, _I, _I, _I, _P]),

@@ -343,6 +343,10 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
   p.gper = p.group;
   p.n_batch = B;
   p.dkv_acc = nullptr;
+  // FA_B200_STAGE_ACCUMULATE: dq is added into (not zeroed), dk/dv are fp32
+  // accumulators the fused kernel adds into
+  const bool accumulate = (stages & FA_B200_STAGE_ACCUMULATE) != 0;
+  p.dkv_reduce = accumulate ? 1 : 0;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
 
@@ -350,8 +354,8 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const long long threads = rows_pad * (D / 8);
     bwd_preprocess_kernel<D, BF><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
         static_cast<const uint16_t*>(o), L.o, static_cast<const uint16_t*>(dO), L.dO, lse, p.dvec,
-        p.lse2, N, n_pad, Hq, rows_pad, p.scale, p.dq_fp32 ? static_cast<float*>(dq) : nullptr,
-        L.dq);
+        p.lse2, N, n_pad, Hq, rows_pad, p.scale,
+        (p.dq_fp32 && !accumulate) ? static_cast<float*>(dq) : nullptr, L.dq);
     if (int st = launch_status("bwd_preprocess_kernel")) return st;
   }
   if (stages & FA_B200_STAGE_DKDV) {
@@ -379,28 +383,37 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const uint64_t units = BHkv * static_cast<uint64_t>(nq128);
     const size_t rows_bytes = 2 * sizeof(float) * static_cast<size_t>(rows_pad);
     const size_t acc_bytes = 2 * sizeof(float) * static_cast<size_t>(BHkv) * N * D;
-    if (p.group > 1 && units < 2ull * sms && ws_bytes >= rows_bytes + acc_bytes) {
+    if (p.group > 1 && units < 2ull * sms && (accumulate || ws_bytes >= rows_bytes + acc_bytes)) {
       const int want = std::min<int>(p.group, static_cast<int>((2ull * sms + units - 1) / units));
       p.gper = (p.group + want - 1) / want;
       p.gsplit = (p.group + p.gper - 1) / p.gper;
     }
-    CUtensorMap tdkv = tdq;   // unused unless the group is split
-    if (p.gsplit > 1) {
+    // fp32 dK / dV accumulators (32-row boxes) for the reduce-add epilogue: the
+    // caller's dk/dv when accumulating, else the workspace of a split group
+    CUtensorMap tdka = tdq, tdva = tdq;   // unused by the 16-bit store epilogue
+    if (accumulate) {
+      if (!make_map4(&tdka, dk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv, B, L.dk, 32) ||
+          !make_map4(&tdva, dv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv, B, L.dv, 32))
+        return FA_B200_ERR_TENSOR_MAP;
+    } else if (p.gsplit > 1) {
+      p.dkv_reduce = 1;
       p.dkv_acc = ws + 2 * rows_pad;
       if (cudaMemsetAsync(p.dkv_acc, 0, acc_bytes, stream) != cudaSuccess)
         return launch_status("the dK/dV accumulator memset");
-      if (!make_map4(&tdkv, p.dkv_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv, 2ull * B,
-                     contiguous(Hkv, N, D), 32))
+      const Strides sacc = contiguous(Hkv, N, D);
+      if (!make_map4(&tdka, p.dkv_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv, B, sacc, 32) ||
+          !make_map4(&tdva, p.dkv_acc + BHkv * N * D, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hkv,
+                     B, sacc, 32))
         return FA_B200_ERR_TENSOR_MAP;
     }
-    CUtensorMap tdk, tdv;   // dK / dV outputs, 64-column x 128-row boxes
-    if (!make_map4(&tdk, dk, dt, 2, D, N, Hkv, B, L.dk, 128) ||
-        !make_map4(&tdv, dv, dt, 2, D, N, Hkv, B, L.dv, 128))
+    CUtensorMap tdk = tdq, tdv = tdq;   // 16-bit dK / dV outputs, 64-column x 128-row boxes
+    if (!accumulate && (!make_map4(&tdk, dk, dt, 2, D, N, Hkv, B, L.dk, 128) ||
+                        !make_map4(&tdv, dv, dt, 2, D, N, Hkv, B, L.dv, 128)))
       return FA_B200_ERR_TENSOR_MAP;
     bwd_fused_kernel<D, BF><<<static_cast<unsigned>(units * p.gsplit), FusedCfg<D>::THREADS,
-                              FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdkv, tdk, tdv, p);
+                              FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdka, tdva, tdk, tdv, p);
     if (int st = launch_status("bwd_fused_kernel")) return st;
-    if (p.gsplit > 1) {
+    if (p.gsplit > 1 && !accumulate) {
       const long long total = 2ll * BHkv * N * (D / 8);
       bwd_dkv_convert_kernel<BF><<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
           p.dkv_acc, p.dk, L.dk, p.dv, L.dv, B, Hkv, N, D, total);
@@ -559,9 +572,13 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
                   size_t workspace_bytes, bool noalloc, int B, int Hq, int Hkv, int N, int D,
                   int dtype, int causal, int stages, const BwdLayout& L, void* stream) {
   if (stages == 0) stages = default_stages(dq_fp32);
-  if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
+  if (stages & ~(FA_B200_STAGE_ALL | FA_B200_STAGE_FUSED | FA_B200_STAGE_ACCUMULATE))
+    return FA_B200_ERR_SHAPE;
   if ((stages & FA_B200_STAGE_FUSED) && (!dq_fp32 || (stages & (FA_B200_STAGE_DKDV | FA_B200_STAGE_DQ))))
     return FA_B200_ERR_SHAPE;
+  // accumulating needs the fused stage (fp32 dq); dk/dv are then fp32
+  const bool accumulate = (stages & FA_B200_STAGE_ACCUMULATE) != 0;
+  if (accumulate && !(stages & FA_B200_STAGE_FUSED)) return FA_B200_ERR_SHAPE;
   if (!q || !k || !v || !dO || !o || !lse || !dq || !dk || !dv) return FA_B200_ERR_NULL_POINTER;
   int st = check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
@@ -584,7 +601,8 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
     if (!aligned16(ptr)) return FA_B200_ERR_ALIGNMENT;
   if ((!noalloc && !aligned16(workspace)) || !strides_ok(L.q, 2) || !strides_ok(L.k, 2) ||
       !strides_ok(L.v, 2) || !strides_ok(L.dO, 2) || !strides_ok(L.o, 2) ||
-      !strides_ok(L.dq, dq_fp32 ? 4 : 2) || !strides_ok(L.dk, 2) || !strides_ok(L.dv, 2))
+      !strides_ok(L.dq, dq_fp32 ? 4 : 2) || !strides_ok(L.dk, accumulate ? 4 : 2) ||
+      !strides_ok(L.dv, accumulate ? 4 : 2))
     return FA_B200_ERR_ALIGNMENT;
   int dev = 0, sms = 0;
   int* err = nullptr;
@@ -643,6 +661,33 @@ size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal) 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaGetLastError();   // a host without a device keeps the default
   return fab::forward_split_bytes(B, Hq, D, fab::forward_split(B, Hq, N, causal, sms));
+}
+
+int fa_b200_merge_partial(float* o, fa_b200_strides so, float* lse, fa_b200_strides slse,
+                          const void* o_part, fa_b200_strides sop, const float* lse_part,
+                          fa_b200_strides slp, int B, int H, int N, int D, int dtype,
+                          void* stream) {
+  if (!o || !lse || !o_part || !lse_part) return FA_B200_ERR_NULL_POINTER;
+  if (D != 64 && D != 128) return FA_B200_ERR_HEAD_DIM;
+  if (B < 1 || H < 1 || N < 1) return FA_B200_ERR_SHAPE;
+  if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
+  const fab::Strides a = fab::from_abi(so), p = fab::from_abi(sop);
+  const fab::Strides la = fab::from_abi(slse), lp = fab::from_abi(slp);
+  if (!fab::aligned16(o) || !fab::aligned16(o_part) || !fab::strides_ok(a, 4) ||
+      !fab::strides_ok(p, 2) || la.b < 0 || la.h < 0 || la.n < 0 || lp.b < 0 || lp.h < 0 ||
+      lp.n < 0)
+    return FA_B200_ERR_ALIGNMENT;
+  const long long total = static_cast<long long>(B) * H * N * (D / 8);
+  if ((total + 255) / 256 > 0x7fffffffll) return FA_B200_ERR_TOO_LARGE;
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (dtype == FA_B200_DTYPE_BF16)
+    fab::merge_partial_kernel<true><<<blocks, 256, 0, s>>>(
+        o, a, lse, la, static_cast<const uint16_t*>(o_part), p, lse_part, lp, H, N, D, total);
+  else
+    fab::merge_partial_kernel<false><<<blocks, 256, 0, s>>>(
+        o, a, lse, la, static_cast<const uint16_t*>(o_part), p, lse_part, lp, H, N, D, total);
+  return fab::launch_status("merge_partial_kernel");
 }
 
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {

@@ -51,6 +51,8 @@ struct BwdParams {
   int gsplit, gper;    // fused kernel: GQA group split over gsplit CTAs of gper heads
   int n_batch;         // B
   float* dkv_acc;      // gsplit > 1: fp32 dK then dV, (2B, Hkv, N, D), added into
+  int dkv_reduce;      // fused kernel: add dK/dV in fp32 into the tm_dka/tm_dva
+                       // accumulators (group split, or a caller accumulating)
   float scale;         // 1/sqrt(D)
   float scale_log2;    // scale * log2(e)
 };
@@ -936,7 +938,8 @@ __global__ void __launch_bounds__(512, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_dq,
-                     const __grid_constant__ CUtensorMap tm_dkv,
+                     const __grid_constant__ CUtensorMap tm_dka,
+                     const __grid_constant__ CUtensorMap tm_dva,
                      const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                      const BwdParams p) {
   using C = FusedCfg<D>;
@@ -1348,7 +1351,7 @@ __global__ void __launch_bounds__(512, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        if (p.gsplit == 1) {
+        if (!p.dkv_reduce) {
           // dV and dK rounded to 16 bits, staged as 64-column swizzled boxes in
           // the idle Q/dO ring (every load and MMA has completed) and written
           // by TMA stores: whole 128-byte rows instead of one row per thread
@@ -1365,10 +1368,11 @@ __global__ void __launch_bounds__(512, 1)
               st_row32_sw128<BF>(s_ring + t * C::TILE + (col / 64) * 16384, r, (col % 64) / 32, x);
             }
         } else {
-          // partial dK/dV of this split: 32-row x 32-column fp32 boxes staged in
-          // the ring and dS tile (idle now: every load and MMA has completed;
-          // the read-out warps' staging buffers lie beyond them) and added into
-          // the fp32 accumulator, dK as batch b and dV as batch B + b
+          // dK/dV added in fp32 into the accumulators of tm_dka / tm_dva (a
+          // split group's partial sums, or a caller accumulating over calls):
+          // 32-row x 32-column boxes staged in the ring and dS tile (idle now:
+          // every load and MMA has completed; the read-out warps' staging
+          // buffers lie beyond them) and added by TMA reduce-adds
           constexpr int NB = D / 64;               // boxes per tensor per warp
           const uint32_t wbox = s_ring + warp * (2 * NB * 4096);
           const int krow0 = kv0 + 32 * (warp & 3);
@@ -1392,15 +1396,15 @@ __global__ void __launch_bounds__(512, 1)
             for (int t = 0; t < 2; ++t)
 #pragma unroll 1
               for (int c = 0; c < NB; ++c)
-                tma_reduce_add_4d(&tm_dkv, wbox + (t * NB + c) * 4096, w * (D / 2) + 32 * c, krow0,
-                                  kvh, t * (p.n_batch) + b);
+                tma_reduce_add_4d(t ? (const void*)&tm_dva : (const void*)&tm_dka,
+                                  wbox + (t * NB + c) * 4096, w * (D / 2) + 32 * c, krow0, kvh, b);
             bulk_commit_group();
             bulk_wait_read_all();   // boxes read: shared memory may be released
           }
         }
       }
     }
-    if (p.gsplit == 1) {
+    if (!p.dkv_reduce) {
       // every compute thread gets here once, whichever path it took above; a
       // thread that skipped its staging raised the abort flag first
       fence_async_smem();

@@ -538,4 +538,51 @@ __global__ void __launch_bounds__(256) fwd_combine_kernel(const float* __restric
   if (part8 == 0) lse[static_cast<size_t>(bh) * n + row] = l;
 }
 
+// Folds one attention result over a further set of keys (16-bit O_p and its
+// LSE_p) into a running fp32 (O, LSE), in place:
+//   LSE' = logaddexp(LSE, LSE_p),  O' = O e^(LSE - LSE') + O_p e^(LSE_p - LSE').
+// The ring's per-step merge, one pass over the rows. One thread per 8 columns;
+// the d/8 threads of a row are lanes of one warp (d/8 divides 32), which read
+// both LSEs before the row's first lane writes the new one. Rows without keys
+// on either side (both LSEs -inf) are left unchanged.
+template <bool BF>
+__global__ void __launch_bounds__(256) merge_partial_kernel(float* __restrict__ o, Strides so,
+                                                            float* __restrict__ lse, Strides sl,
+                                                            const uint16_t* __restrict__ op,
+                                                            Strides sop,
+                                                            const float* __restrict__ lsep,
+                                                            Strides slp, int h, int n, int d,
+                                                            long long total) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const bool live = i < total;
+  const int per_row = d / 8;
+  const long long row = live ? i / per_row : 0;
+  const int part8 = static_cast<int>(i - row * per_row);
+  const int r = static_cast<int>(row % n);
+  const long long bh = row / n;
+  const int hh = static_cast<int>(bh % h), bb = static_cast<int>(bh / h);
+  float la = -INFINITY, lp = -INFINITY;
+  if (live) {
+    la = lse[sl.at(bb, hh, r)];
+    lp = lsep[slp.at(bb, hh, r)];
+  }
+  __syncwarp();
+  const float m = fmaxf(la, lp);
+  if (!live || m == -INFINITY) return;
+  const float l = m + log1pf(expf(-fabsf(la - lp)));
+  const float wa = expf(la - l), wp = expf(lp - l);
+  float4* a = reinterpret_cast<float4*>(o + so.at(bb, hh, r)) + 2 * part8;
+  const uint4 pk = reinterpret_cast<const uint4*>(op + sop.at(bb, hh, r))[part8];
+  const float2 p0 = unpack2<BF>(pk.x), p1 = unpack2<BF>(pk.y), p2 = unpack2<BF>(pk.z),
+               p3 = unpack2<BF>(pk.w);
+  float4 a0 = a[0], a1 = a[1];
+  a0 = make_float4(a0.x * wa + p0.x * wp, a0.y * wa + p0.y * wp, a0.z * wa + p1.x * wp,
+                   a0.w * wa + p1.y * wp);
+  a1 = make_float4(a1.x * wa + p2.x * wp, a1.y * wa + p2.y * wp, a1.z * wa + p3.x * wp,
+                   a1.w * wa + p3.y * wp);
+  a[0] = a0;
+  a[1] = a1;
+  if (part8 == 0) lse[sl.at(bb, hh, r)] = l;
+}
+
 }  // namespace fab

@@ -25,7 +25,11 @@ at their owner after G hops. Transfers are double-buffered: the next step's
 K/V are in flight while the current step computes.
 
 The per-piece attention functions are injectable (`ops`), so the ring logic
-runs on CPU ranks (gloo) in tests; the default ops are the CUDA kernels.
+runs on CPU ranks (gloo) in tests; the default ops are the CUDA kernels, which
+also do the merge (one pass, fa_b200_merge_partial) and add each piece's
+gradients straight into the fp32 dq and travelling dK/dV accumulators
+(FA_B200_STAGE_ACCUMULATE), and read the pieces' Q/K/V/dO/O halves in place.
+Ops without `merge` / `bwd_acc` get the plain torch versions below.
 """
 import math
 
@@ -97,6 +101,16 @@ class CudaOps:
         dq, dk, dv = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
         return dq, dk.float(), dv.float()
 
+    @staticmethod
+    def merge(o_acc, lse_acc, o_p, lse_p):
+        import fa_p100_ext
+        fa_p100_ext.merge_partial(o_acc, lse_acc, o_p, lse_p)
+
+    @staticmethod
+    def bwd_acc(q, k, v, do, o, lse, causal, dq, dk, dv):
+        import fa_p100_ext
+        fa_p100_ext.backward_accumulate(q, k, v, do, o, lse, causal, dq, dk, dv)
+
 
 def _merge(o_acc, lse_acc, o_p, lse_p):
     """Fold one piece (O_p, LSE_p) into the running fp32 (O, LSE), in place."""
@@ -132,13 +146,13 @@ def ring_forward(q, k, v, ops=CudaOps, group=None):
         nxt = None
         if step + 1 < world:
             nxt = _exchange(kv, group, world, rank)
+        merge = getattr(ops, "merge", _merge)
         for qh, kh, causal in ring_pieces(world, rank, step):
-            o_p, lse_p = ops.fwd(_half(q, qh).contiguous(), _half(kv[0], kh).contiguous(),
-                                 _half(kv[1], kh).contiguous(), causal)
+            o_p, lse_p = ops.fwd(_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), causal)
             if o_acc is None:
                 o_acc, lse_acc = o_p.float(), lse_p.float().clone()
                 continue
-            _merge(_half(o_acc, qh), _half(lse_acc, qh), o_p, lse_p)
+            merge(_half(o_acc, qh), _half(lse_acc, qh), o_p, lse_p)
         if nxt is not None:
             bufs, works = nxt
             for w in works:
@@ -163,10 +177,12 @@ def ring_backward(q, k, v, do, o, lse, ops=CudaOps, group=None):
         dk_s = torch.zeros(kv[0].shape, dtype=torch.float32, device=q.device)
         dv_s = torch.zeros_like(dk_s)
         for qh, kh, causal in ring_pieces(world, rank, step):
-            dq_p, dk_p, dv_p = ops.bwd(_half(q, qh).contiguous(), _half(kv[0], kh).contiguous(),
-                                       _half(kv[1], kh).contiguous(), _half(do, qh).contiguous(),
-                                       _half(o, qh).contiguous(), _half(lse, qh).contiguous(),
-                                       causal)
+            args = (_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), _half(do, qh), _half(o, qh),
+                    _half(lse, qh), causal)
+            if hasattr(ops, "bwd_acc"):
+                ops.bwd_acc(*args, _half(dq, qh), _half(dk_s, kh), _half(dv_s, kh))
+                continue
+            dq_p, dk_p, dv_p = ops.bwd(*args)
             _half(dq, qh).add_(dq_p)
             _half(dk_s, kh).add_(dk_p)
             _half(dv_s, kh).add_(dv_p)

@@ -168,6 +168,69 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, 
     return [dq, dk, dv]
 
 
+def backward_accumulate(q, k, v, dO, o, lse, causal, dq, dk, dv):
+    """Adds this call's gradients into fp32 accumulators: dq (B,Hq,N,D), dk,
+    dv (B,Hkv,N,D), any layout with a contiguous D axis (views of larger
+    accumulators included). One fused pass (FA_B200_STAGE_ACCUMULATE): dQ and
+    dK/dV are added by TMA reduce-adds, so nothing is rounded to 16 bits
+    between calls. For callers that sum gradients over several calls, as ring
+    attention does over its steps. Returns (dq, dk, dv)."""
+    for t, name in ((q, "q"), (dO, "dO"), (k, "k"), (v, "v"), (o, "o")):
+        _check_in(t, name)
+    if lse.dtype != torch.float32 or not lse.is_cuda:
+        raise RuntimeError("lse must be a CUDA fp32 tensor")
+    B, H, Hkv, N, D = _shapes(q, k, v)
+    if dO.shape != q.shape or o.shape != q.shape or lse.shape != (B, H, N):
+        raise RuntimeError("dO and o must match q, and lse must be (B, Hq, N)")
+    dtype = _dtype_code(q, k, v, dO, o)
+    (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
+    (dO, sdo), (o, so) = _layout(dO), _layout(o)
+    lse = lse.contiguous()
+    dq, sdq = _out(dq, (B, H, N, D), torch.float32, q.device, "dq")
+    dk, sdk = _out(dk, (B, Hkv, N, D), torch.float32, q.device, "dk")
+    dv, sdv = _out(dv, (B, Hkv, N, D), torch.float32, q.device, "dv")
+    lib = _lib.lib()
+    ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
+    ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
+    stages = 1 | 8 | 16   # FA_B200_STAGE_ROWSUM | FUSED | ACCUMULATE
+    with torch.cuda.device(q.device):
+        st = lib.fa_b200_backward_strided(
+            q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, dO.data_ptr(), sdo,
+            o.data_ptr(), so, lse.data_ptr(), dq.data_ptr(), sdq, 1, dk.data_ptr(), sdk,
+            dv.data_ptr(), sdv, ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, dtype,
+            1 if causal else 0, stages, _stream_ptr(q.device))
+    _lib.check(st, "fa_b200_backward_strided (accumulate)")
+    return dq, dk, dv
+
+
+def merge_partial(o, lse, o_part, lse_part):
+    """In place: o (fp32, B,H,N,D) and lse (fp32, B,H,N) -- attention over one
+    set of keys -- absorb o_part (16-bit) and lse_part, the same queries over
+    other keys: lse = logaddexp(lse, lse_part), o = o e^(lse_old - lse) +
+    o_part e^(lse_part - lse). Views (e.g. half of a longer accumulator) are
+    fine."""
+    _check_in(o_part, "o_part")
+    B, H, N, D = o_part.shape
+    if o.dtype != torch.float32 or tuple(o.shape) != (B, H, N, D) or o.device != o_part.device:
+        raise RuntimeError("o must be an fp32 tensor shaped like o_part on its device")
+    for t, name in ((lse, "lse"), (lse_part, "lse_part")):
+        if t.dtype != torch.float32 or tuple(t.shape) != (B, H, N) or t.device != o_part.device:
+            raise RuntimeError(f"{name} must be an fp32 (B, H, N) tensor on o_part's device")
+    so = _lib.strides_of(o)
+    if so is None:
+        raise RuntimeError("o: the D axis must be contiguous and the base and strides 16-byte aligned")
+    o_part, sop = _layout(o_part)
+    sl = _lib.Strides(*lse.stride())
+    slp = _lib.Strides(*lse_part.stride())
+    dtype = _lib.DTYPE_BF16 if o_part.dtype == torch.bfloat16 else _lib.DTYPE_FP16
+    with torch.cuda.device(o.device):
+        st = _lib.lib().fa_b200_merge_partial(o.data_ptr(), so, lse.data_ptr(), sl,
+                                              o_part.data_ptr(), sop, lse_part.data_ptr(), slp,
+                                              B, H, N, D, dtype, _stream_ptr(o.device))
+    _lib.check(st, "fa_b200_merge_partial")
+    return o, lse
+
+
 def backward(q, k, v, dO, o, lse, causal):
     """dq fp32 (B,Hq,N,D), dk, dv in q's dtype (B,Hkv,N,D). fa_p100_ext.cu:103-142."""
     return backward_into(q, k, v, dO, o, lse, causal, torch.float32)

@@ -114,6 +114,23 @@ int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO
                      size_t workspace_bytes, int B, int Hq, int Hkv, int N, int D, int causal,
                      void* stream);
 
+/* Folds an attention result over a further set of keys into a running one,
+ * in place: with o/lse the fp32 output and natural-log LSE so far and
+ * o_part/lse_part (16-bit `dtype` output and its LSE) the same queries'
+ * attention over other keys,
+ *   lse <- logaddexp(lse, lse_part),
+ *   o   <- o e^(lse_old - lse) + o_part e^(lse_part - lse).
+ * Rows whose two LSEs are both -inf are left unchanged. The step that combines
+ * the pieces of context-parallel (ring) attention; one pass over the rows.
+ * o (float, strides in floats) and o_part are (B, H, N, D) with D contiguous
+ * (D 64 or 128), 16-byte aligned bases and strides; lse and lse_part are
+ * (B, H, N) with any strides. No counterpart in the reference, which has no
+ * multi-GPU attention. */
+int fa_b200_merge_partial(float* o, fa_b200_strides so, float* lse, fa_b200_strides slse,
+                          const void* o_part, fa_b200_strides sop, const float* lse_part,
+                          fa_b200_strides slp, int B, int H, int N, int D, int dtype,
+                          void* stream);
+
 /* Stages of the backward, for fa_b200_backward_stages. */
 enum {
   FA_B200_STAGE_ROWSUM = 1,  /* Dv = rowsum(dO o O) into the workspace; also zeroes an
@@ -121,11 +138,18 @@ enum {
   FA_B200_STAGE_DKDV = 2,    /* dK, dV (reads the workspace) */
   FA_B200_STAGE_DQ = 4,      /* dQ (reads the workspace) */
   FA_B200_STAGE_ALL = 7,      /* ROWSUM | DKDV | DQ: the deterministic set */
-  FA_B200_STAGE_FUSED = 8     /* dK, dV and dQ in one kernel, dQ added by TMA reduce-adds
+  FA_B200_STAGE_FUSED = 8,    /* dK, dV and dQ in one kernel, dQ added by TMA reduce-adds
                                * into a zeroed fp32 dq (the reference's accumulate-into-
                                * fp32 scheme); needs dq_fp32 and a prior ROWSUM stage
                                * (which zeroes dq); excludes DKDV and DQ. Not bitwise
                                * deterministic; the default for dq_fp32 != 0 */
+  FA_B200_STAGE_ACCUMULATE = 16 /* with FUSED (and dq_fp32): add this call's gradients to
+                               * the contents of dq, dk and dv instead of overwriting
+                               * them -- ROWSUM does not zero dq, and dk, dv are fp32
+                               * accumulators (float*, strides in floats) that dK and
+                               * dV are added into by TMA reduce-adds. For callers that
+                               * sum gradients over several calls (context-parallel
+                               * rings, chunked sequences). */
 };
 
 /* fa_b200_backward restricted to the stages in `stages`. The dK/dV and dQ

@@ -134,6 +134,27 @@ def test_strided_backward_argument_errors():
     assert bwd_strided(stages=8, dq_fp32=0) == 3     # the fused stage needs an fp32 dq
     assert bwd_strided(stages=64) == 3
     assert bwd_strided(dtype=7) == 11
+    # accumulating (stage 16) needs the fused stage and an fp32 dq
+    assert bwd_strided(stages=16) == 3
+    assert bwd_strided(stages=1 | 16) == 3
+    assert bwd_strided(stages=1 | 8 | 16, dq_fp32=0) == 3
+
+
+def merge(o=P, lse=P, op=P, lp=P, D=64, dtype=0, so=None, sop=None, B=1):
+    lib = _lib.lib()
+    return lib.fa_b200_merge_partial(o, so or S(), lse, S(), op, sop or S(), lp, S(), B, 4, 16, D,
+                                     dtype, None)
+
+
+def test_merge_partial_argument_errors():
+    assert merge(o=None) == 1
+    assert merge(lp=None) == 1
+    assert merge(D=96) == 2
+    assert merge(B=0) == 3
+    assert merge(dtype=3) == 11
+    assert merge(o=MISALIGNED) == 4
+    assert merge(so=S(n=66)) == 4          # fp32 rows: strides in multiples of 4 floats
+    assert merge(sop=S(n=68)) == 4         # 16-bit rows: multiples of 8 elements
 
 
 def test_strides_of_layouts():

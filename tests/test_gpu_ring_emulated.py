@@ -1,0 +1,151 @@
+"""Ring context parallelism on ONE GPU: every rank of a 2- or 4-way ring runs
+as a thread of this process (ring_forward / ring_backward with a stand-in
+group) and the NCCL point-to-point exchange is replaced by an in-process
+mailbox, so the whole ring -- the CUDA ops for the pieces, the
+fused LSE merge and the accumulating backward -- runs and is checked against
+the single-GPU kernel on the whole sequence without a second GPU. Also checks
+the two ring ops on their own: fa_b200_merge_partial and the accumulating
+backward stage."""
+import threading
+
+import pytest
+import torch
+
+import fa_b200_ring as ring
+import fa_p100
+import fa_p100_ext
+from oracle import attention_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+class _Group:
+    """Stands in for a process group: each rank's thread passes its own."""
+
+    def __init__(self, world, rank):
+        self.world, self.rank = world, rank
+
+
+class _GroupDist:
+    """get_world_size / get_rank of a _Group (the ring reads nothing else)."""
+
+    @staticmethod
+    def get_world_size(group=None):
+        return group.world
+
+    @staticmethod
+    def get_rank(group=None):
+        return group.rank
+
+
+class _Mailbox:
+    """Send to rank+1, receive from rank-1: the sender enqueues copies on the
+    shared stream before posting them, so the receiver's later kernels see them."""
+
+    def __init__(self, world):
+        self.cv = threading.Condition()
+        self.box = {r: [] for r in range(world)}
+
+    def exchange(self, tensors, group, world, rank):
+        copies = [t.clone() for t in tensors]
+        with self.cv:
+            self.box[(rank + 1) % world].append(copies)
+            self.cv.notify_all()
+        me = rank
+
+        class _Work:
+            def __init__(self, mb):
+                self.mb, self.got = mb, None
+
+            def wait(self):
+                if self.got is None:
+                    with self.mb.cv:
+                        self.mb.cv.wait_for(lambda: self.mb.box[me], timeout=60)
+                        self.got = self.mb.box[me].pop(0)
+                    for dst, src in zip(recv, self.got):
+                        dst.copy_(src)
+
+        recv = [torch.empty_like(t) for t in tensors]
+        return recv, [_Work(self)]
+
+
+def _run_ring(world, full, monkeypatch):
+    mb = _Mailbox(world)
+    monkeypatch.setattr(ring, "dist", _GroupDist)
+    monkeypatch.setattr(ring, "_exchange", mb.exchange)
+    out, errs = {}, []
+
+    def rank_main(rank):
+        try:
+            # ring_forward / ring_backward directly: autograd would run every
+            # rank's backward on one device thread, where the ranks wait on
+            # each other
+            grp = _Group(world, rank)
+            q, k, v, do = [ring.zigzag_shard(t, world, rank) for t in full]
+            o_acc, lse = ring.ring_forward(q, k, v, ring.CudaOps, grp)
+            o = o_acc.to(q.dtype)
+            dq, dk, dv = ring.ring_backward(q, k, v, do, o, lse, ring.CudaOps, grp)
+            out[rank] = [t.float() for t in (o, dq, dk, dv)]
+        except Exception as e:   # surfaced below
+            errs.append(e)
+
+    threads = [threading.Thread(target=rank_main, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    torch.cuda.synchronize()
+    if errs:
+        raise errs[0]
+    return [ring.zigzag_unshard([out[r][i] for r in range(world)]) for i in range(4)]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_emulated_ring_matches_single_gpu(cuda, world, monkeypatch):
+    B, Hq, Hkv, N, D = 1, 8, 2, 4096, 128
+    full = [t.to(cuda) for t in orc.seeded_inputs(B, Hq, Hkv, N, D, seed=21)]
+    a = [t.clone().requires_grad_(True) for t in full[:3]]
+    o1 = fa_p100.flash_attn(*a, True)     # also loads the library before the threads start
+    o1.backward(full[3])
+    single = [o1.detach().float()] + [t.grad.float() for t in a]
+    got = _run_ring(world, full, monkeypatch)
+    for name, g, s in zip(("O", "dQ", "dK", "dV"), got, single):
+        err = orc.frob_rel(g, s)
+        print(f"world {world} {name}: ring vs single-GPU frob rel {err:.2e}")
+        assert err < 5e-3, name
+
+
+def test_merge_partial_matches_formula(cuda):
+    g = torch.Generator(device=cuda).manual_seed(3)
+    B, H, N, D = 2, 3, 300, 128
+    big = torch.randn(B, H, 2 * N, D, device=cuda, generator=g)
+    lse_big = torch.randn(B, H, 2 * N, device=cuda, generator=g) * 3
+    o_acc, lse_acc = big[:, :, N:], lse_big[:, :, N:]          # views, as the ring passes
+    o_p = torch.randn(B, H, N, D, device=cuda, generator=g).half()
+    lse_p = torch.randn(B, H, N, device=cuda, generator=g) * 3
+    lse_p[0, 0, :7] = -float("inf")                             # rows with no keys in the piece
+    ref_l = torch.logaddexp(lse_acc, lse_p)
+    ref_o = o_acc * torch.exp(lse_acc - ref_l)[..., None] + o_p.float() * torch.exp(lse_p - ref_l)[..., None]
+    fa_p100_ext.merge_partial(o_acc, lse_acc, o_p, lse_p)
+    assert torch.allclose(lse_acc, ref_l, rtol=1e-6, atol=1e-6)
+    assert (o_acc - ref_o).abs().max().item() < 1e-5 * ref_o.abs().max().item() + 1e-6
+    assert torch.equal(big[:, :, :N], big[:, :, :N])            # untouched half (sanity)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal", [(1, 4, 2, 777, 128, True), (2, 2, 2, 300, 64, False),
+                                               (1, 16, 1, 1000, 64, True)])
+def test_backward_accumulate_adds(cuda, B, Hq, Hkv, N, D, causal):
+    q, k, v, do = orc.seeded_inputs(B, Hq, Hkv, N, D, seed=5, device=cuda)
+    o, lse = fa_p100_ext.forward(q, k, v, causal)
+    ref = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
+    g = torch.Generator(device=cuda).manual_seed(9)
+    # accumulators: halves of wider fp32 buffers (strided, as the ring's are)
+    bufs = [torch.randn(B, h, N, 2 * D, device=cuda, generator=g) for h in (Hq, Hkv, Hkv)]
+    acc = [b_[..., D:] for b_ in bufs]
+    start = [a.clone() for a in acc]
+    fa_p100_ext.backward_accumulate(q, k, v, do, o, lse, causal, *acc)
+    for name, a, s, r in zip(("dq", "dk", "dv"), acc, start, ref):
+        err = orc.frob_rel(a - s, r.float())
+        assert err < 2e-3, (name, err)
+    import _lib
+    assert _lib.device_error(0) == 0
