@@ -874,25 +874,25 @@ namespace fab {
 // (setmaxnreg): compute 160, read-out 144, the MMA/TMA warpgroup 48; per lane
 // of an SMSP 160 + 160 + 144 + 48 = 512 = the 4 x 128 launched.
 // TMEM: S^T 0..127, with P^T (fp16 pairs) written back over cols 32..95 |
-//       dP^T 128..255, with dS^T (fp16 pairs) written back over cols 160..223,
-//       then (D = 128) dQ_i | dV 256.. | dK 256+D.. | (D = 64) dQ 384..
+//       dP^T 128..255, then (D = 128) dQ_i | dV 256.. | dK 256+D.. |
+//       (D = 64) dQ 384..
 // Shared: K, V, a 2-slot Q ring and a 1-slot (D = 64: 2-slot) dO ring, the dS
 // tile [key][query], two 4 KiB dQ staging boxes per read-out warp, LSE/Dv
 // slices for two steps.
 // MMA order per step i (brackets = what it waits for):
 //   [P_i] dV_i = P^T dO (A in TMEM) ; [Q_{i+1}] S^T_{i+1} ;
-//   [dS_i] dK_i = dS^T Q (A in TMEM), dQ_i = dS K (A = the dS tile read
-//   MN-major, into the dP^T columns, after dK_i has read dS^T there) ;
+//   [dS_i] dQ_i = dS K (A = the dS tile read MN-major, into the dP^T
+//   columns), dK_i = dS^T Q (A = the same tile read K-major) ;
 //   [dQ_i read, dO_{i+1}] dP^T_{i+1}   (D = 128; with D = 64 dQ has columns
 //   of its own and the dQ_i read gates dQ_{i+1} instead)
 // and the compute warps run dS_i, then P_{i+1}, so that the P phase of the
-// next step overlaps dK_i and dQ_i on the tensor core; the read-out warps take
-// dQ_i off the tensor memory as soon as it is complete.
+// next step overlaps dQ_i and dK_i on the tensor core; the read-out warps take
+// dQ_i off the tensor memory while dK_i runs, so dP^T_{i+1} rarely waits.
 // Overwrites follow issue order (S^T_{i+1} after dV_i read P_i; dQ_i after
 // the compute threads read dP_i; dP^T_{i+1} after the read-out warps read
 // dQ_i). The dS
 // tile is rewritten for step i+1 only after dP^T_{i+1} completed, which was
-// issued after dK_i and dQ_i. The Q slot of step i is released after dK_i,
+// issued after dQ_i and dK_i. The Q slot of step i is released after dK_i,
 // so the LSE/Dv slice buffer i & 1, loaded with Q, is reloaded (for step i+2)
 // only after every compute thread finished step i; the dO slot of step i is
 // released after dV_i, which gives the load of dO_{i+1} the rest of step i.
@@ -930,7 +930,7 @@ struct FusedCfg {
   // waits for it to be read out; D = 64 leaves columns 384.. free for a dQ of
   // its own, and only dQ_{i+1} waits for the read-out of dQ_i.
   static constexpr bool DQ_OWN_COLS = (D == 64);
-  static constexpr uint32_t COL_P = 32, COL_DS = 160, COL_DQ = DQ_OWN_COLS ? 384 : 128;
+  static constexpr uint32_t COL_P = 32, COL_DQ = DQ_OWN_COLS ? 384 : 128;
 };
 
 template <int D, bool BF>
@@ -1098,7 +1098,7 @@ __global__ void __launch_bounds__(512, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && total > 0) {
       constexpr uint32_t id_t = idesc_f16(128, 128, false, false, BF);  // S^T, dP^T
-      constexpr uint32_t id_g = idesc_f16(128, D, false, true, BF);     // dV, dK (TS)
+      constexpr uint32_t id_g = idesc_f16(128, D, false, true, BF);     // dV (TS), dK (SS)
       constexpr uint32_t id_q = idesc_f16(128, D, true, true, BF);      // dQ: A = dS MN-major
       // X^T = (K or V) (Q or dO)^T: 128 x 128, K = D
       auto issue_t = [&](uint32_t d_tmem, uint32_t a_s, uint32_t b_s_) {
@@ -1110,7 +1110,8 @@ __global__ void __launch_bounds__(512, 1)
         }
       };
       auto slot_addr = [&](int slot) { return s_ring + slot * C::TILE; };
-      const uint64_t d_dsm = sdesc_sw128(s_ds, 16384, 1024);    // dS tile as MN-major A
+      const uint64_t d_dsm = sdesc_sw128(s_ds, 16384, 1024);    // dS tile as MN-major A (dQ)
+      const uint64_t d_dsk = sdesc_sw128(s_ds, 16, 1024);       // dS^T, K-major A (dK)
       const uint64_t d_kmn = sdesc_sw128(s_k, 16384, 1024);     // K as MN-major B
       bool ok = mbar_wait(b_kv, 0, ctl, kErrTimeoutMma);
       if (ok) ok = mbar_wait(b_full + 8 * q_slot(0), q_ph(0), ctl, kErrTimeoutMma);
@@ -1148,18 +1149,12 @@ __global__ void __launch_bounds__(512, 1)
           issue_t(tmem + C::COL_S, s_k, slot_addr(q_slot(i + 1)));
           mma_commit(b_s);
         }
-        // dK_i += dS_i^T Q_i ; dQ_i = dS_i K
+        // dQ_i = dS_i K, then dK_i += dS_i^T Q_i, both reading dS_i from the
+        // shared tile: dQ_i completes first, so its read-out overlaps dK_i and
+        // dP^T_{i+1} (which reuses the dQ_i columns when D = 128) need not wait
         ok = mbar_wait(b_ds, i & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        {
-          const uint64_t dq_mn = sdesc_sw128(slot_addr(q_slot(i)), 16384, 1024);
-#pragma unroll
-          for (int kk = 0; kk < C::BM / 16; ++kk)
-            mma_ts(tmem + C::COL_DK, tmem + C::COL_DS + kk * 8, sdesc_add(dq_mn, kk * 2048), id_g,
-                   (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(b_empty + 8 * q_slot(i));
         if (C::DQ_OWN_COLS && i > 0) {   // dQ_{i-1} has been read out of its columns
           ok = mbar_wait(b_dqfree, (i - 1) & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
@@ -1170,6 +1165,14 @@ __global__ void __launch_bounds__(512, 1)
           mma_ss(tmem + C::COL_DQ, sdesc_add(d_dsm, kk * 2048), sdesc_add(d_kmn, kk * 2048), id_q,
                  kk > 0 ? 1u : 0u);
         mma_commit(b_dqfull);
+        {
+          const uint64_t dq_mn = sdesc_sw128(slot_addr(q_slot(i)), 16384, 1024);
+#pragma unroll
+          for (int kk = 0; kk < C::BM / 16; ++kk)
+            mma_ss(tmem + C::COL_DK, sdesc_add(d_dsk, (kk >> 2) * 16384 + (kk & 3) * 32),
+                   sdesc_add(dq_mn, kk * 2048), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(b_empty + 8 * q_slot(i));
         if (more) {
           ok = (C::DQ_OWN_COLS || mbar_wait(b_dqfree, i & 1, ctl, kErrTimeoutMma)) &&
                mbar_wait(b_full + 8 * o_slot(i + 1), o_ph(i + 1), ctl, kErrTimeoutMma);
@@ -1329,12 +1332,11 @@ __global__ void __launch_bounds__(512, 1)
             pv[h][c + 1] = ds.y;
           }
         }
-      // dS^T as fp16 pairs over dP^T columns this group has read (A of dK)
-      tmem_st_pairs<BF>(tmem + C::COL_DS + 32 * w + lane_off, pv);
+      // dS^T rows into the shared [key][query] tile, the A operand of dK
+      // (K-major) and of dQ (MN-major)
       st_row32_sw128<BF>(s_ds + w * 16384, r, 0, pv[0]);
       st_row32_sw128<BF>(s_ds + w * 16384, r, 1, pv[1]);
       fence_async_smem();
-      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_ds);
       return true;
