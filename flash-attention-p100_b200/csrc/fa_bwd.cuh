@@ -1194,9 +1194,10 @@ __global__ void __launch_bounds__(512, 1)
     // columns, frees the columns for dP^T_{i+1}, then stages its D/32 boxes of
     // 32 x 32 fp32 through two alternating 4 KiB buffers and adds each into dQ
     // with a TMA reduce-add. Before staging a box the warp waits until the TMA
-    // unit has read all its earlier boxes: each warp keeps at most one box in
-    // the queue that the Q/dO tile loads share (measured faster than letting
-    // both buffers fill), and a warp with no rows below N stages nothing.
+    // unit has read the box staged two earlier in the same buffer, so each
+    // warp keeps at most two boxes queued (the L2 accepts the adds slowly, and
+    // a warp that waited for each box before staging the next fell behind the
+    // tensor core); a warp with no rows below N stages nothing.
     const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t stg = sbase + C::OFF_STG + (warp - 8) * 8192;
@@ -1224,7 +1225,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
       for (int h = 0; h < NB; ++h) {
         const uint32_t box = stg + (h & 1) * 4096;
-        if (lane == 0) bulk_wait_read_all();   // at most one box of this warp in the TMA queue
+        if (lane == 0) bulk_wait_read_all_but_last();   // the buffer's previous box has been read
         __syncwarp();
 #pragma unroll
         for (int c = 0; c < 8; ++c)
