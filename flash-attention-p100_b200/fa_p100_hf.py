@@ -15,8 +15,9 @@ Contract kept from the reference (fa_p100_hf.py:46-213):
     dropout, head_dim outside {64, 128}, a scale other than 1/sqrt(D), and
     q_len != kv_len (a populated KV cache);
   * fp16 inputs run as they are, and so (beyond the reference) do bf16 ones;
-    other dtypes are cast to fp16, silently under fp16 autocast and with a
-    single warning otherwise; the output is cast back to the input dtype.
+    other dtypes (or a mix) are cast to the autocast dtype under fp16 or bf16
+    autocast, and to fp16 with a single warning outside autocast; the output is
+    cast back to the input dtype.
 """
 import warnings
 
@@ -68,21 +69,25 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
         is_causal = bool(getattr(module, "is_causal", True)) and query.size(2) > 1
 
     in_dtype = query.dtype
-    # fp16 (the reference's type) and bf16 run as they are; anything else
-    # (fp32, or a mix) is cast to fp16 as the reference does
+    # fp16 (the reference's type) and bf16 run as they are; anything else (fp32,
+    # or a mix -- Qwen3's q/k leave their fp32 RMSNorm weights in fp32 even under
+    # autocast) is cast to the autocast dtype when autocast is on, as SDPA's
+    # inputs would be, and otherwise to fp16 as the reference does
     native = all(t.dtype == torch.float16 for t in (query, key, value)) or all(
         t.dtype == torch.bfloat16 for t in (query, key, value))
     if not native:
-        under_fp16_autocast = (torch.is_autocast_enabled("cuda")
-                               and torch.get_autocast_dtype("cuda") == torch.float16)
-        if not under_fp16_autocast and not _warned_cast:
+        autocast = torch.is_autocast_enabled("cuda")
+        target = torch.get_autocast_dtype("cuda") if autocast else torch.float16
+        if target not in (torch.float16, torch.bfloat16):
+            target = torch.float16
+        if not autocast and not _warned_cast:
             warnings.warn(
                 f"fa_p100: casting q={query.dtype} k={key.dtype} v={value.dtype} to "
-                "float16 outside fp16 autocast (the kernel computes in fp16); wrap "
-                "the step in torch.autocast('cuda', torch.float16)",
+                "float16 outside autocast (the kernel computes in fp16 or bf16); wrap "
+                "the step in torch.autocast('cuda', torch.float16 or torch.bfloat16)",
                 stacklevel=2)
             _warned_cast = True
-        query, key, value = query.half(), key.half(), value.half()
+        query, key, value = query.to(target), key.to(target), value.to(target)
 
     # output straight in (B, N, H, D), the layout fa_p100_hf.py:142 transposes to
     out = flash_attn_bnhd(query, key, value, causal=bool(is_causal),

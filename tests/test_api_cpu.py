@@ -91,3 +91,19 @@ def test_register_and_enable():
         model(ids, use_cache=True)
     # idempotent: enabling twice keeps a single guard
     assert fa_p100_hf.enable_fa_p100(model) is model
+
+
+def test_finetune_harness_host_parts():
+    """The harness's data and model description, without a GPU: synthetic
+    blocks are reproducible, the default model is Qwen3-0.6B's architecture,
+    and the CLI defaults follow the reference's (seq 2048, 30 steps, 3 warm-up,
+    8 blocks, 8 loss chunks)."""
+    import finetune_hf
+    a = finetune_hf.synthetic_blocks(1000, 64, 3, seed=4)
+    b = finetune_hf.synthetic_blocks(1000, 64, 3, seed=4)
+    assert a.shape == (3, 64) and (a == b).all() and a.max() < 1000
+    cfg = finetune_hf.qwen3_0p6b_config()
+    assert (cfg.num_hidden_layers, cfg.hidden_size, cfg.num_attention_heads,
+            cfg.num_key_value_heads, cfg.head_dim, cfg.vocab_size) == (28, 1024, 16, 8, 128, 151936)
+    args = finetune_hf.parser().parse_args([])
+    assert (args.seq_len, args.steps, args.warmup, args.blocks, args.loss_chunks) == (2048, 30, 3, 8, 8)
