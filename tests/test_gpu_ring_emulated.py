@@ -149,3 +149,24 @@ def test_backward_accumulate_adds(cuda, B, Hq, Hkv, N, D, causal):
         assert err < 2e-3, (name, err)
     import _lib
     assert _lib.device_error(0) == 0
+
+
+def test_emulated_ring_c5_full_length(cuda, monkeypatch):
+    """BASELINE config 5 at its full length (B=1, Hq=32, Hkv=8, N=131072,
+    D=128, causal): the 8-way zigzag ring against the single-GPU kernel on the
+    whole sequence -- the C5 correctness check (the CPU oracle cannot hold the
+    N^2 scores at this length; the ring matches it at small N in
+    test_emulated_ring_matches_single_gpu and tests/test_ring_cpu.py)."""
+    B, Hq, Hkv, N, D = 1, 32, 8, 131072, 128
+    g = torch.Generator(device=cuda).manual_seed(31)
+    full = [torch.randn(B, h, N, D, device=cuda, generator=g).half() for h in (Hq, Hkv, Hkv, Hq)]
+    a = [t.clone().requires_grad_(True) for t in full[:3]]
+    o1 = fa_p100.flash_attn(*a, True)
+    o1.backward(full[3])
+    single = [o1.detach()] + [t.grad for t in a]
+    del a, o1
+    got = _run_ring(8, full, monkeypatch)
+    for name, gt, s in zip(("O", "dQ", "dK", "dV"), got, single):
+        err = orc.frob_rel(gt, s.float())
+        print(f"C5 {name}: 8-way ring vs single-GPU frob rel {err:.2e}")
+        assert err < 5e-3, name
