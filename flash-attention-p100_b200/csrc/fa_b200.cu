@@ -384,8 +384,19 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     const size_t rows_bytes = 2 * sizeof(float) * static_cast<size_t>(rows_pad);
     const size_t acc_bytes = 2 * sizeof(float) * static_cast<size_t>(BHkv) * N * D;
     if (p.group > 1 && units < 2ull * sms && (accumulate || ws_bytes >= rows_bytes + acc_bytes)) {
-      const int want = std::min<int>(p.group, static_cast<int>((2ull * sms + units - 1) / units));
-      p.gper = (p.group + want - 1) / want;
+      // heads per CTA: the fewest waves of CTAs times the work of each (gper
+      // heads plus a quarter head of fixed cost per CTA); more parts mean more
+      // fp32 dK/dV partials to add, which are small at these sizes
+      double best = 1e30;
+      for (int gp = 1; gp <= p.group; ++gp) {
+        const uint64_t parts = (p.group + gp - 1) / gp;
+        const uint64_t waves = (units * parts + sms - 1) / sms;
+        const double cost = static_cast<double>(waves) * (gp + 0.25);
+        if (cost < best) {
+          best = cost;
+          p.gper = gp;
+        }
+      }
       p.gsplit = (p.group + p.gper - 1) / p.gper;
     }
     // fp32 dK / dV accumulators (32-row boxes) for the reduce-add epilogue: the
