@@ -330,12 +330,7 @@ def run_ours(args, world, rank, local):
     ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
     ws = torch.empty(ws_bytes // 4, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
-    # the forward's workspace (a key-range split of its heaviest query blocks
-    # when the grid is small; none otherwise)
     sq, skv = _lib.strides_of(q), _lib.strides_of(k)
-    fws_bytes = lib.fa_b200_forward_workspace_bytes(B, Hq, N, D, int(causal))
-    fws = torch.empty(max(fws_bytes // 4, 1), device=dev)
-    fws_ptr = fws.data_ptr() if fws_bytes else None
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     ev = {n: [] for n in KERNELS}
@@ -354,7 +349,7 @@ def run_ours(args, world, rank, local):
             marks[0].record(stream)
         st = lib.fa_b200_forward_strided(q.data_ptr(), sq, k.data_ptr(), skv, v.data_ptr(), skv,
                                          o.data_ptr(), sq, lse.data_ptr(), B, Hq, Hkv, N, D,
-                                         _lib.DTYPE_FP16, int(causal), 0, fws_ptr, fws_bytes, sp)
+                                         _lib.DTYPE_FP16, int(causal), 0, None, 0, sp)
         _lib.check(st, "fa_b200_forward_strided")
         for i, mask in enumerate(STAGES):
             if record:

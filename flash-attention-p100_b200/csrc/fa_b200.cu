@@ -79,6 +79,8 @@ template <bool BF>
 void set_smem_all() {
   set_smem(fwd_kernel<64, BF>, FwdCfg<64>::SMEM);
   set_smem(fwd_kernel<128, BF>, FwdCfg<128>::SMEM);
+  set_smem(fwd_kernel_s<64, BF>, FwdCfgS<64>::SMEM);
+  set_smem(fwd_kernel_s<128, BF>, FwdCfgS<128>::SMEM);
   set_smem(bwd_dkdv_kernel<64, BF>, DkdvCfg<64>::SMEM);
   set_smem(bwd_dkdv_kernel<128, BF>, DkdvCfg<128>::SMEM);
   set_smem(bwd_dq_kernel<64, BF>, DqCfg<64>::SMEM);
@@ -237,26 +239,16 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
   return FA_B200_OK;
 }
 
-// How many of each head's top m-blocks (256 query rows) the forward splits
-// into two key-range halves: none unless the (B*Hq, m-block) grid leaves SMs
-// idle; then all m-blocks whose two query tiles both have keys in both halves
-// (causal: every m-block but the first; else all, given two key blocks).
-int forward_split(int B, int Hq, int N, int causal, int sms) {
-  const long long mblocks = (N + 255) / 256;
-  if (static_cast<long long>(B) * Hq * mblocks >= sms) return 0;
-  if (causal) return static_cast<int>(mblocks - 1);
-  return (N + 127) / 128 >= 2 ? static_cast<int>(mblocks) : 0;
-}
-
-size_t forward_split_bytes(int B, int Hq, int D, int n_split) {
-  return 2 * static_cast<size_t>(B) * Hq * n_split * 256 * (D + 1) * sizeof(float);
+// The two-tile forward (256 query rows per CTA) when its grid fills the GPU,
+// else the small-grid one (128 rows per CTA, 256-key steps).
+bool forward_small_grid(int B, int Hq, int N, int sms) {
+  return static_cast<long long>(B) * Hq * ((N + 255) / 256) < sms;
 }
 
 template <int D, bool BF>
 int launch_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                   int Hkv, int N, int causal, const FwdLayout& L, void* ws, size_t ws_bytes,
-                   int sms, cudaStream_t stream, int* err) {
-  using C = FwdCfg<D>;
+                   int Hkv, int N, int causal, const FwdLayout& L, int sms, cudaStream_t stream,
+                   int* err) {
   CUtensorMap tq, tk, tv;
   const uint64_t BH = static_cast<uint64_t>(B) * Hq;
   const CUtensorMapDataType dt = BF ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -273,30 +265,22 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
   p.hq = Hq;
   p.group = Hq / Hkv;
   p.causal = causal ? 1 : 0;
-  p.n_mblocks = (N + 255) / 256;
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)) * 1.4426950408889634);
-  p.n_split = 0;
-  p.opart = p.lpart = nullptr;
-  if (p.n_mblocks > 32767 || BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-  const int n_split = forward_split(B, Hq, N, causal, sms);
-  if (n_split > 0 && ws && ws_bytes >= forward_split_bytes(B, Hq, D, n_split)) {
-    p.n_split = n_split;
-    p.opart = static_cast<float*>(ws);
-    p.lpart = p.opart + 2 * BH * n_split * 256 * D;
-  }
-  dim3 grid(static_cast<unsigned>(BH), p.n_mblocks + p.n_split);
+  if (BH > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
   CUtensorMap to;   // O output, 64-column x 128-row boxes
   if (!make_map4(&to, o, dt, 2, D, N, Hq, B, L.o, 128)) return FA_B200_ERR_TENSOR_MAP;
-  fwd_kernel<D, BF><<<grid, C::THREADS, C::SMEM, stream>>>(tq, tk, tv, to, p);
-  if (int st = launch_status("fwd_kernel")) return st;
-  if (p.n_split > 0) {
-    const long long total = static_cast<long long>(BH) * p.n_split * 256 * (D / 8);
-    fwd_combine_kernel<D, BF><<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-        p.opart, p.lpart, p.o, p.so, lse, N, Hq, p.n_mblocks, p.n_split,
-        static_cast<int>(BH), total);
-    return launch_status("fwd_combine_kernel");
+  if (forward_small_grid(B, Hq, N, sms)) {
+    p.n_mblocks = (N + 127) / 128;
+    if (p.n_mblocks > 65535) return FA_B200_ERR_TOO_LARGE;
+    fwd_kernel_s<D, BF><<<dim3(static_cast<unsigned>(BH), p.n_mblocks), FwdCfgS<D>::THREADS,
+                          FwdCfgS<D>::SMEM, stream>>>(tq, tk, tv, to, p);
+    return launch_status("fwd_kernel_s");
   }
-  return FA_B200_OK;
+  p.n_mblocks = (N + 255) / 256;
+  if (p.n_mblocks > 65535) return FA_B200_ERR_TOO_LARGE;
+  fwd_kernel<D, BF><<<dim3(static_cast<unsigned>(BH), p.n_mblocks), FwdCfg<D>::THREADS,
+                      FwdCfg<D>::SMEM, stream>>>(tq, tk, tv, to, p);
+  return launch_status("fwd_kernel");
 }
 
 template <int D, bool BF>
@@ -564,6 +548,7 @@ int forward_impl(const void* q, const void* k, const void* v, void* o, float* ls
       (ws && !aligned16(ws)) || !strides_ok(L.q, 2) || !strides_ok(L.k, 2) ||
       !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
     return FA_B200_ERR_ALIGNMENT;
+  (void)ws_bytes;   // the forward needs no workspace (kept in the ABI)
   int dev = 0, sms = 0;
   int* err = nullptr;
   st = device_setup(&dev, &err, &sms);
@@ -571,7 +556,7 @@ int forward_impl(const void* q, const void* k, const void* v, void* o, float* ls
   auto s = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == FA_B200_DTYPE_BF16;
 #define FAB_FWD(DD, BB) \
-  launch_forward<DD, BB>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, ws, ws_bytes, sms, s, err)
+  launch_forward<DD, BB>(q, k, v, o, lse, B, Hq, Hkv, N, causal, L, sms, s, err)
   if (D == 64) return bf ? FAB_FWD(64, true) : FAB_FWD(64, false);
   return bf ? FAB_FWD(128, true) : FAB_FWD(128, false);
 #undef FAB_FWD
@@ -666,12 +651,8 @@ int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa
 }
 
 size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal) {
-  if (B < 1 || Hq < 1 || N < 1 || D < 1) return 0;
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaGetLastError();   // a host without a device keeps the default
-  return fab::forward_split_bytes(B, Hq, D, fab::forward_split(B, Hq, N, causal, sms));
+  (void)B, (void)Hq, (void)N, (void)D, (void)causal;
+  return 0;   // small grids run a kernel of their own; nothing to split or merge
 }
 
 int fa_b200_merge_partial(float* o, fa_b200_strides so, float* lse, fa_b200_strides slse,

@@ -7,8 +7,12 @@
 // (:127-130), LSE = m + ln(l) in natural log (:321-330), GQA head mapping
 // kv_head = q_head / group (:87-92).
 //
-// Structure of one CTA (persistent over nothing: one CTA = 256 query rows of
-// one (batch, q-head)):
+// Two kernels, chosen by grid size (launch_forward): fwd_kernel below, one CTA
+// per 256 query rows, when B*Hq*ceil(N/256) fills the GPU; fwd_kernel_s (further
+// down) with one CTA per 128 rows and 256-key steps when it would not.
+//
+// fwd_kernel -- structure of one CTA (one CTA = 256 query rows of one
+// (batch, q-head)):
 //   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): two warpgroups,
 //               thread r of group h takes row r, columns 64h .. 64h+63
 //   warps 8-15  softmax for query tile 1 (rows m0+128 .. m0+255), the same way
@@ -46,16 +50,9 @@ struct FwdParams {
   int hq;           // query heads
   int group;        // hq / hkv
   int causal;
-  int n_mblocks;    // ceil(N / 256)
+  int n_mblocks;    // m-blocks of the launched kernel: ceil(N / 256), or ceil(N / 128)
+                    // for the small-grid kernel
   float scale_log2; // softmax scale * log2(e)
-  // Key-range split for small grids: the n_split heaviest m-blocks of every
-  // head are done by two CTAs each (key blocks [0, half) and [half, end)),
-  // which write fp32 O (normalized by their own row sums) and LSE to opart /
-  // lpart, [part][B*Hq][n_split][256 rows] (x D for O); fwd_combine_kernel
-  // merges them.
-  int n_split;
-  float* opart;
-  float* lpart;
 };
 
 template <int D>
@@ -132,13 +129,9 @@ __global__ void __maxnreg__(96)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (B*Hq, m-blocks + split halves): every head's longest causal rows
-  // are dispatched first; y < 2*n_split are the two key-range halves of the
-  // n_split top m-blocks, the rest their unsplit m-blocks, top down
+  // grid (B*Hq, m-blocks): every head's longest causal rows are dispatched first
   const int bh = blockIdx.x;
-  const int y = static_cast<int>(blockIdx.y);
-  const int part = y < 2 * p.n_split ? (y & 1) : -1;
-  const int mb = p.n_mblocks - 1 - (part >= 0 ? y / 2 : y - p.n_split);
+  const int mb = p.n_mblocks - 1 - static_cast<int>(blockIdx.y);
   const int m0 = mb * 256;
   // tensor-map coordinates: query head / batch, and the kv head it reads
   const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
@@ -148,19 +141,6 @@ __global__ void __maxnreg__(96)
   for (int t = 0; t < 2; ++t) {
     const int r0 = m0 + 128 * t;
     ntile[t] = (r0 >= p.n) ? 0 : (p.causal ? min(nblk, r0 / 128 + 1) : nblk);
-  }
-  // this CTA's key blocks [jb, je); ntile[] and nkv count from jb
-  int jb = 0;
-  {
-    const int full = max(ntile[0], ntile[1]);
-    int je = full;
-    if (part >= 0) {
-      const int half = full / 2;
-      jb = part ? half : 0;
-      je = part ? full : half;
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t) ntile[t] = max(0, min(je, ntile[t]) - jb);
   }
   const int nkv = max(ntile[0], ntile[1]);
   const Ctl ctl{abort_flag, p.err};
@@ -204,14 +184,14 @@ __global__ void __maxnreg__(96)
       constexpr int kAhead = 2;  // L2 prefetch distance, in key blocks
       for (int j = 0; j < kAhead && j < nkv; ++j)
         for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_4d(&tm_k, c * 64, (jb + j) * 128, hk_i, b_i);
-          tma_prefetch_l2_4d(&tm_v, c * 64, (jb + j) * 128, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_k, c * 64, j * 128, hk_i, b_i);
+          tma_prefetch_l2_4d(&tm_v, c * 64, j * 128, hk_i, b_i);
         }
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + kAhead < nkv)
           for (int c = 0; c < C::CH; ++c) {
-            tma_prefetch_l2_4d(&tm_k, c * 64, (jb + j + kAhead) * 128, hk_i, b_i);
-            tma_prefetch_l2_4d(&tm_v, c * 64, (jb + j + kAhead) * 128, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_k, c * 64, (j + kAhead) * 128, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_v, c * 64, (j + kAhead) * 128, hk_i, b_i);
           }
 #pragma unroll 1
         for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
@@ -225,7 +205,7 @@ __global__ void __maxnreg__(96)
 #pragma unroll
           for (int c = 0; c < C::CH; ++c)
             tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
-                        c * 64, (jb + j) * 128, hk_i, b_i);
+                        c * 64, j * 128, hk_i, b_i);
         }
       }
       // Drain: do not leave the CTA while a load it issued may still land.
@@ -334,7 +314,7 @@ __global__ void __maxnreg__(96)
 #pragma unroll
         for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
       float* s = reinterpret_cast<float*>(&sr[0][0]);
-      const int kb0 = (jb + j) * 128;   // this step's first key
+      const int kb0 = j * 128;   // this step's first key
       const int col0 = kb0 + c0;
       const bool need_mask = (kb0 + 128 > p.n) || (p.causal && kb0 + 127 > m0 + 128 * t);
       if (need_mask) {
@@ -343,12 +323,13 @@ __global__ void __maxnreg__(96)
         for (int c = 0; c < 64; ++c)
           if (col0 + c > lim) s[c] = -INFINITY;
       }
-      // this half's max: 8 interleaved chains of three-input maxima, then a tree
+      // this half's max: 8 interleaved chains of three-input maxima over
+      // s[16..63], seeded with s[0..15], then a tree
       float mx8[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) mx8[c] = s[c];
+      for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(s[c], s[c + 8]);
 #pragma unroll
-      for (int c = 8; c < 64; c += 16)
+      for (int c = 16; c < 64; c += 16)
 #pragma unroll
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
       const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
@@ -427,26 +408,6 @@ __global__ void __maxnreg__(96)
         tc_fence_after();
         const float inv = 1.f / l;
         const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
-        if (part >= 0) {   // a key-range half: fp32 partial O and LSE for the combine
-          const size_t prow = ((static_cast<size_t>(part) * gridDim.x + bh) * p.n_split +
-                               (mb - (p.n_mblocks - p.n_split))) * 256 + 128 * t + r;
-          float* og = p.opart + prow * D + hf * (D / 2);
-#pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t orow[32];
-            tmem_ld32(t_o + hf * (D / 2) + 32 * c, orow);
-            tmem_ld_wait(orow);
-            if (row < p.n) {
-#pragma unroll
-              for (int v = 0; v < 8; ++v)
-                reinterpret_cast<float4*>(og + 32 * c)[v] =
-                    make_float4(__uint_as_float(orow[4 * v]) * inv, __uint_as_float(orow[4 * v + 1]) * inv,
-                                __uint_as_float(orow[4 * v + 2]) * inv,
-                                __uint_as_float(orow[4 * v + 3]) * inv);
-            }
-          }
-          if (row < p.n && hf == 0) p.lpart[prow] = (m_used + __log2f(l)) * 0.69314718055994531f;
-        } else {
         // O rows rounded to 16 bits, staged as 64-column swizzled boxes over
         // this tile's Q (every MMA that reads Q_t has completed) and written
         // by TMA stores below
@@ -468,21 +429,18 @@ __global__ void __maxnreg__(96)
           }
         }
         if (row < p.n && hf == 0) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
-        }
       }
     }
-    if (part < 0) {
-      // every thread of the tile gets here once, whichever path it took above;
-      // a thread that skipped its staging raised the abort flag first
-      fence_async_smem();
-      named_bar_sync(1 + t, 256);
-      if ((threadIdx.x & 255) == 0 && nt > 0 && *abort_flag == 0) {
+    // every thread of the tile gets here once, whichever path it took above;
+    // a thread that skipped its staging raised the abort flag first
+    fence_async_smem();
+    named_bar_sync(1 + t, 256);
+    if ((threadIdx.x & 255) == 0 && nt > 0 && *abort_flag == 0) {
 #pragma unroll 1
-        for (int c = 0; c < D / 64; ++c)
-          tma_store_4d(&tm_o, (t ? s_q1 : s_q0) + c * 16384, 64 * c, m0 + 128 * t, hq_i, b_i);
-        bulk_commit_group();
-        bulk_wait_read_all();   // boxes read: shared memory may be released
-      }
+      for (int c = 0; c < D / 64; ++c)
+        tma_store_4d(&tm_o, (t ? s_q1 : s_q0) + c * 16384, 64 * c, m0 + 128 * t, hq_i, b_i);
+      bulk_commit_group();
+      bulk_wait_read_all();   // boxes read: shared memory may be released
     }
   }
 
@@ -499,44 +457,379 @@ __global__ void __maxnreg__(96)
 
 namespace fab {
 
-// Merges the two key-range halves of the split m-blocks: per row
-// LSE = log(e^LSE_0 + e^LSE_1) and O = O_0 e^(LSE_0 - LSE) + O_1 e^(LSE_1 - LSE),
-// written as the final 16-bit O (strides so) and LSE. One thread per 8 columns.
+// ---------------------------------------------------------------------------
+// Small-grid forward: one CTA per 128 query rows (twice the CTAs of the
+// two-tile kernel, for grids that would leave SMs idle), keys in steps of 256:
+//   warps 0-7   softmax: thread r of half h owns row r and keys 128h .. 128h+127
+//               of each step; the halves exchange row maxima and sums
+//   warp  8     TMEM allocation + MMA issue;  warp 9  TMA loads
+// TMEM: S [0,256) fp32 | P [256,384) fp16 pairs of the step's 256 keys | O [384, 384+D).
+// P has columns of its own, so S of step j+1 (one N = 256 MMA) is issued as soon
+// as the softmax has read S of step j and runs while its exponentials do;
+// O += P V (A from TMEM) once P is stored, and P is rewritten only after that
+// product has completed. Shared memory: Q, two K steps, one V step.
+// ---------------------------------------------------------------------------
+template <int D>
+struct FwdCfgS {
+  static constexpr int BM = 128;                // query rows per CTA
+  static constexpr int BN = 256;                // keys per step (one S MMA of N = 256)
+  static constexpr int CH = D / 64;             // 64-column chunks per row
+  static constexpr int QBYTES = BM * D * 2;
+  static constexpr int KVBYTES = BN * D * 2;    // one step of K or V: [chunk][256 rows][128 B]
+  static constexpr int CHUNK = BN * 128;        // bytes of one 64-column chunk of a step tile
+  static constexpr int KS = 2, VS = 1;          // K steps / V steps resident
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_RING = OFF_Q + QBYTES;
+  static constexpr int OFF_X = OFF_RING + (KS + VS) * KVBYTES;  // [parity][half][row] floats
+  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 128 * 4;
+  // barriers: q, full[KS+VS], empty[KS+VS], s, sfree, p, pv, o, x
+  static constexpr int NBAR = 1 + 2 * (KS + VS) + 6;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;   // window must start 1024-aligned
+  static_assert(SMEM <= 232448, "shared memory over the per-block limit");
+  static constexpr int THREADS = 320;
+  static constexpr int MMA_WARP = 8, TMA_WARP = 9;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
+};
+
+}  // namespace fab
+
+namespace fab {
+
+// S[tmem] = Q (128 x D, K-major) * K_step^T (256 x D, K-major): N = 256
 template <int D, bool BF>
-__global__ void __launch_bounds__(256) fwd_combine_kernel(const float* __restrict__ opart,
-                                                          const float* __restrict__ lpart,
-                                                          uint16_t* __restrict__ o, Strides so,
-                                                          float* __restrict__ lse, int n, int hq,
-                                                          int n_mblocks, int n_split, int bhs,
-                                                          long long total) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  constexpr int PER_ROW = D / 8;
-  const long long prow = i / PER_ROW;                   // over (B*Hq, n_split, 256)
-  const int part8 = static_cast<int>(i - prow * PER_ROW);
-  const int lrow = static_cast<int>(prow % 256);
-  const long long bm = prow / 256;
-  const int ms = static_cast<int>(bm % n_split);
-  const int bh = static_cast<int>(bm / n_split);
-  const int row = (n_mblocks - n_split + ms) * 256 + lrow;
-  if (row >= n) return;
-  const long long half = static_cast<long long>(bhs) * n_split * 256;   // rows of one part
-  const float l0 = lpart[prow], l1 = lpart[half + prow];
-  const float m = fmaxf(l0, l1);
-  const float l = m + logf(expf(l0 - m) + expf(l1 - m));
-  const float w0 = expf(l0 - l), w1 = expf(l1 - l);
-  const float4* a = reinterpret_cast<const float4*>(opart + prow * D) + 2 * part8;
-  const float4* c = reinterpret_cast<const float4*>(opart + (half + prow) * D) + 2 * part8;
-  const float4 a0 = a[0], a1 = a[1], c0 = c[0], c1 = c[1];
-  uint4 pk;
-  pk.x = pack2<BF>(a0.x * w0 + c0.x * w1, a0.y * w0 + c0.y * w1);
-  pk.y = pack2<BF>(a0.z * w0 + c0.z * w1, a0.w * w0 + c0.w * w1);
-  pk.z = pack2<BF>(a1.x * w0 + c1.x * w1, a1.y * w0 + c1.y * w1);
-  pk.w = pack2<BF>(a1.z * w0 + c1.z * w1, a1.w * w0 + c1.w * w1);
-  const int b = bh / hq, h = bh % hq;
-  reinterpret_cast<uint4*>(o + so.at(b, h, row))[part8] = pk;
-  if (part8 == 0) lse[static_cast<size_t>(bh) * n + row] = l;
+__device__ __forceinline__ void issue_qk256(uint32_t d_tmem, uint32_t q_s, uint32_t k_s) {
+  using C = FwdCfgS<D>;
+  constexpr uint32_t idesc = idesc_f16(128, 256, false, false, BF);
+  const uint64_t dq = sdesc_sw128(q_s, 16, 1024), dk = sdesc_sw128(k_s, 16, 1024);
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk)
+    mma_ss(d_tmem, sdesc_add(dq, (kk >> 2) * 16384 + (kk & 3) * 32),
+           sdesc_add(dk, (kk >> 2) * C::CHUNK + (kk & 3) * 32), idesc, kk > 0 ? 1u : 0u);
 }
+// O[tmem] (+)= P (128 x 256 keys, fp16 pairs in TMEM) * V_step (256 keys x D, MN-major)
+template <int D, bool BF>
+__device__ __forceinline__ void issue_pv256(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_s,
+                                         bool accumulate) {
+  using C = FwdCfgS<D>;
+  constexpr uint32_t idesc = idesc_f16(128, D, false, true, BF);
+  const uint64_t dv = sdesc_sw128(v_s, C::CHUNK, 1024);
+#pragma unroll
+  for (int kk = 0; kk < 256 / 16; ++kk)
+    mma_ts(d_tmem, p_tmem + kk * 8, sdesc_add(dv, kk * 2048), idesc,
+           (accumulate || kk > 0) ? 1u : 0u);
+}
+
+template <int D, bool BF>
+__global__ void __launch_bounds__(320, 1)
+    fwd_kernel_s(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+               const FwdParams p) {
+  using C = FwdCfgS<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (!smem_aligned_or_report(smem_raw, p.err)) return;
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t s_q = sbase + C::OFF_Q, s_ring = sbase + C::OFF_RING;
+  const uint32_t b_q = sbase + C::OFF_BAR;
+  const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * (C::KS + C::VS);
+  const uint32_t b_s = b_empty + 8 * (C::KS + C::VS), b_sfree = b_s + 8, b_p = b_sfree + 8,
+                 b_pv = b_p + 8, b_o = b_pv + 8, b_x = b_o + 8;
+  float* xbuf = reinterpret_cast<float*>(smem_raw + C::OFF_X);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // grid (B*Hq, 128-row m-blocks): every head's longest causal rows first
+  const int bh = blockIdx.x;
+  const int mb = p.n_mblocks - 1 - static_cast<int>(blockIdx.y);
+  const int m0 = mb * C::BM;
+  const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
+  // keys [0, kend): causal rows see keys up to their own row
+  const int kend = p.causal ? min(p.n, m0 + C::BM) : p.n;
+  const int nstep = (kend + C::BN - 1) / C::BN;
+  const Ctl ctl{abort_flag, p.err};
+  auto k_slot = [](int j) { return j % C::KS; };
+  auto k_ph = [](int j) { return static_cast<uint32_t>((j / C::KS) & 1); };
+  auto v_slot = [](int j) { return C::KS + j % C::VS; };
+  auto v_ph = [](int j) { return static_cast<uint32_t>((j / C::VS) & 1); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(b_q, 1);
+    for (int s = 0; s < C::KS + C::VS; ++s) {
+      mbar_init(b_full + 8 * s, 1);
+      mbar_init(b_empty + 8 * s, 1);
+    }
+    mbar_init(b_s, 1);
+    mbar_init(b_sfree, 256);
+    mbar_init(b_p, 256);
+    mbar_init(b_pv, 1);
+    mbar_init(b_o, 1);
+    mbar_init(b_x, 256);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == C::MMA_WARP) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == C::TMA_WARP) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(b_q, C::QBYTES);
+#pragma unroll
+      for (int c = 0; c < C::CH; ++c) tma_load_4d(s_q + c * 16384, &tm_q, b_q, c * 64, m0, hq_i, b_i);
+      bool ok = true;
+      int nk = 0, nv = 0;
+      // one step of K (kind 0) or V (kind 1): 256 keys as two 128-row boxes per chunk
+      auto issue_step = [&](int kind, int j) -> bool {
+        const int slot = kind ? v_slot(j) : k_slot(j);
+        const uint32_t ph = kind ? v_ph(j) : k_ph(j);
+        if (!mbar_wait(b_empty + 8 * slot, ph ^ 1, ctl, kErrTimeoutLoad)) return false;
+        const uint32_t fb = b_full + 8 * slot;
+        mbar_arrive_expect_tx(fb, C::KVBYTES);
+        const uint32_t dst = s_ring + slot * C::KVBYTES;
+#pragma unroll
+        for (int c = 0; c < C::CH; ++c)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_4d(dst + c * C::CHUNK + h * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k,
+                        fb, c * 64, j * C::BN + 128 * h, hk_i, b_i);
+        if (kind) ++nv; else ++nk;
+        return true;
+      };
+      constexpr int kAhead = 1;  // L2 prefetch distance, in steps
+      auto prefetch = [&](int j) {
+        for (int c = 0; c < C::CH; ++c)
+          for (int h = 0; h < 2; ++h) {
+            tma_prefetch_l2_4d(&tm_k, c * 64, j * C::BN + 128 * h, hk_i, b_i);
+            tma_prefetch_l2_4d(&tm_v, c * 64, j * C::BN + 128 * h, hk_i, b_i);
+          }
+      };
+      for (int j = 0; j < kAhead && j < nstep; ++j) prefetch(j);
+      // K runs one step ahead of V: K_0, then K_{j+1} before V_j
+      for (int j = 0; j < nstep && ok; ++j) {
+        if (j + kAhead < nstep) prefetch(j + kAhead);
+        if (j == 0) ok = issue_step(0, 0);
+        if (ok && j + 1 < nstep) ok = issue_step(0, j + 1);
+        if (ok) ok = issue_step(1, j);
+      }
+      if (!ok) {
+        drain_loads(b_q, 1, 1);
+        drain_loads(b_full, nk, C::KS);
+        drain_loads(b_full + 8 * C::KS, nv, C::VS);
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(b_q, 0, ctl, kErrTimeoutMma) &&
+                mbar_wait(b_full + 8 * k_slot(0), k_ph(0), ctl, kErrTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_qk256<D, BF>(tmem + C::COL_S, s_q, s_ring + k_slot(0) * C::KVBYTES);
+        mma_commit(b_s);
+        mma_commit(b_empty + 8 * k_slot(0));
+      }
+      for (int j = 0; j < nstep && ok; ++j) {
+        // S(j+1) as soon as the softmax has read S(j)
+        if (j + 1 < nstep) {
+          ok = mbar_wait(b_full + 8 * k_slot(j + 1), k_ph(j + 1), ctl, kErrTimeoutMma) &&
+               mbar_wait(b_sfree, j & 1, ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk256<D, BF>(tmem + C::COL_S, s_q, s_ring + k_slot(j + 1) * C::KVBYTES);
+          mma_commit(b_s);
+          mma_commit(b_empty + 8 * k_slot(j + 1));
+        }
+        // O += P(j) V_j
+        ok = mbar_wait(b_full + 8 * v_slot(j), v_ph(j), ctl, kErrTimeoutMma) &&
+             mbar_wait(b_p, j & 1, ctl, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv256<D, BF>(tmem + C::COL_O, tmem + C::COL_P, s_ring + v_slot(j) * C::KVBYTES, j > 0);
+        mma_commit(b_pv);
+        mma_commit(b_empty + 8 * v_slot(j));
+        if (j + 1 == nstep) mma_commit(b_o);
+      }
+      // every MMA issued above completes before TMEM is released
+      const uint64_t t0 = globaltimer_ns();
+      if (nstep > 0)
+        while (!mbar_try_wait(b_pv, (nstep - 1) & 1) && globaltimer_ns() - t0 < FAB_WAIT_LIMIT_NS) {
+        }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    // thread r of half h owns row r and keys 128h .. 128h+127 of each step
+    const int h = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const int row = m0 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + C::COL_S + 128 * h + lane_off;
+    const uint32_t t_p = tmem + C::COL_P + 64 * h + lane_off;
+    const uint32_t t_o = tmem + C::COL_O + (D / 2) * h + lane_off;
+    auto xslot = [&](int par, int half) { return xbuf + (par * 2 + half) * 128 + r; };
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nstep; ++j) {
+      ok = mbar_wait(b_s, j & 1, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, sr[c]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+      tc_fence_before();
+      mbar_arrive(b_sfree);   // S(j+1) may overwrite the S columns now
+      float* s = reinterpret_cast<float*>(&sr[0][0]);
+      const int kb0 = j * C::BN + 128 * h;   // this thread's first key of the step
+      const bool need_mask = (kb0 + 127 >= kend) || (p.causal && kb0 + 127 > m0);
+      if (need_mask) {
+        const int lim = p.causal ? min(kend - 1, row) : (kend - 1);
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (kb0 + c > lim) s[c] = -INFINITY;
+      }
+      float mx8[8];   // as in fwd_kernel, over this half's 128 keys
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(s[c], s[c + 8]);
+#pragma unroll
+      for (int c = 16; c < 128; c += 16)
+#pragma unroll
+        for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
+      const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
+                              max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
+      // the other half of the row's maximum (buffer by step parity)
+      *xslot(j & 1, h) = pmx;
+      mbar_arrive(b_x);
+      ok = mbar_wait(b_x, j & 1, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const float mx = fmaxf(pmx, *xslot(j & 1, h ^ 1));
+      const float m_new = fmaxf(m_used, mx * p.scale_log2);
+      // rescale only when the running max grew by more than 2^8 (P stays below
+      // 256; the final 1/l uses the same offset); warp-wide because O is
+      // rescaled through TMEM, alpha = 1 for rows that do not need it
+      bool rescale = false;
+      float alpha = 1.f;
+      if (j == 0) {
+        m_used = m_new;
+      } else {
+        const bool need = m_new > m_used + 8.f;
+        rescale = __any_sync(0xffffffffu, need);
+        if (need) {
+          alpha = ex2(m_used - m_new);
+          l *= alpha;
+          m_used = m_new;
+        }
+      }
+      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
+      uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
+      uint32_t pk[64];
+#pragma unroll
+      for (int q2 = 0; q2 < 64; ++q2) {
+        const float2 x = f32x2_split(fma_x2(f32x2(s[2 * q2], s[2 * q2 + 1]), sl2, nm));
+        const float e0 = ex2(x.x), e1 = ex2(x.y);
+        lp[q2 & 1] = add_x2(lp[q2 & 1], f32x2(e0, e1));
+        pk[q2] = pack2<BF>(e0, e1);
+      }
+      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
+      l += la.x + la.y;
+      // O += P(j-1) V must be complete before P and O are rewritten
+      if (j > 0) {
+        ok = mbar_wait(b_pv, (j - 1) & 1, ctl, kErrTimeoutSoftmax);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (rescale) {   // this half's D/2 columns of the O row
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t orow[32];
+          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld_wait(orow);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+          tmem_st32(t_o + 32 * c, orow);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = pk[16 * c + i];
+        tmem_st16(t_p + 16 * c, w);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(b_p);
+    }
+    if (ok && nstep > 0) {
+      // the row sum is the two halves' sums: one more exchange (phase nstep)
+      *xslot(nstep & 1, h) = l;
+      mbar_arrive(b_x);
+      ok = mbar_wait(b_x, nstep & 1, ctl, kErrTimeoutSoftmax) &&
+           mbar_wait(b_o, 0, ctl, kErrTimeoutSoftmax);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        l += *xslot(nstep & 1, h ^ 1);
+        tc_fence_after();
+        const float inv = 1.f / l;
+        // O row rounded to 16 bits, staged as 64-column swizzled boxes over the
+        // Q tile (the last S has read it) and written by TMA stores below
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          const int col = (D / 2) * h + 32 * c;
+          uint32_t orow[32];
+          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld_wait(orow);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int piece = 4 * ((col % 64) / 32) + q4;
+            st_shared_v4(s_q + (col / 64) * 16384 + r * 128 + ((piece ^ (r & 7)) << 4),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 0]) * inv, __uint_as_float(orow[8 * q4 + 1]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 2]) * inv, __uint_as_float(orow[8 * q4 + 3]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 4]) * inv, __uint_as_float(orow[8 * q4 + 5]) * inv),
+                         pack2<BF>(__uint_as_float(orow[8 * q4 + 6]) * inv, __uint_as_float(orow[8 * q4 + 7]) * inv));
+          }
+        }
+        if (row < p.n && h == 0)
+          p.lse[static_cast<size_t>(bh) * p.n + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
+      }
+    }
+    // every softmax thread gets here once, whichever path it took above; a
+    // thread that skipped its staging raised the abort flag first
+    fence_async_smem();
+    named_bar_sync(1, 256);
+    if (threadIdx.x == 0 && nstep > 0 && *abort_flag == 0) {
+#pragma unroll 1
+      for (int c = 0; c < D / 64; ++c) tma_store_4d(&tm_o, s_q + c * 16384, 64 * c, m0, hq_i, b_i);
+      bulk_commit_group();
+      bulk_wait_read_all();   // boxes read: shared memory may be released
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == C::MMA_WARP) {
+    __syncwarp();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fab
+
+namespace fab {
 
 // Folds one attention result over a further set of keys (16-bit O_p and its
 // LSE_p) into a running fp32 (O, LSE), in place:

@@ -88,19 +88,6 @@ def _out(t, shape, dtype, device, name):
     return t, st
 
 
-_fwd_ws_sizes = {}
-
-
-def _forward_workspace_bytes(lib, B, H, N, D, causal, device):
-    """fa_b200_forward_workspace_bytes, cached per shape and device (it only
-    depends on them and the device's SM count)."""
-    key = (B, H, N, D, bool(causal), device)
-    size = _fwd_ws_sizes.get(key)
-    if size is None:
-        size = _fwd_ws_sizes[key] = lib.fa_b200_forward_workspace_bytes(B, H, N, D, 1 if causal else 0)
-    return size
-
-
 def forward(q, k, v, causal, full_precision=False, o=None):
     """O (B,Hq,N,D) in q's dtype and LSE (B,Hq,N) fp32 (natural log).
     fa_p100_ext.cu:53-83. q, k, v are fp16 (the reference's type) or bf16; `o`
@@ -115,14 +102,10 @@ def forward(q, k, v, causal, full_precision=False, o=None):
     lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
     lib = _lib.lib()
     with torch.cuda.device(q.device):
-        # key-range split of the heaviest query blocks when the grid is small
-        ws_bytes = _forward_workspace_bytes(lib, B, H, N, D, causal, q.device)
-        ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32) if ws_bytes else None
         st = lib.fa_b200_forward_strided(
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, o.data_ptr(), so,
             lse.data_ptr(), B, H, Hkv, N, D, dtype, 1 if causal else 0,
-            1 if full_precision else 0, ws.data_ptr() if ws is not None else None, ws_bytes,
-            _stream_ptr(q.device))
+            1 if full_precision else 0, None, 0, _stream_ptr(q.device))
     _lib.check(st, "fa_b200_forward_strided")
     return [o, lse]
 

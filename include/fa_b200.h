@@ -77,13 +77,12 @@ int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa
                             int causal, int full_precision, void* workspace,
                             size_t workspace_bytes, void* stream);
 
-/* Workspace that lets fa_b200_forward_strided split the key range of its
- * heaviest query blocks over two CTAs when B*Hq*ceil(N/256) blocks leave SMs
- * of the current device idle (short sequences, few heads); 0 when it would not
- * split. The halves' fp32 partial O and LSE are merged by a second kernel (by
- * logaddexp, so the output matches the unsplit one to fp32 rounding). A
- * forward given less workspace (or none: NULL, 0) does not split. No
- * counterpart in the reference, one block per query tile (flash_fwd.cuh:127). */
+/* Workspace fa_b200_forward_strided needs: 0. Kept for callers written against
+ * an earlier version of this library, whose forward split the key range of
+ * small grids and merged the halves through a workspace; small grids (B*Hq*
+ * ceil(N/256) below the SM count) now run a kernel of their own with one CTA
+ * per 128 query rows. fa_b200_forward_strided accepts and ignores a workspace.
+ * No counterpart in the reference. */
 size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal);
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum

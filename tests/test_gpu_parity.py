@@ -161,28 +161,42 @@ def test_gqa_group_split_matches_unsplit(cuda, B, Hq, Hkv, N, D):
     assert _lib.device_error(0) == 0
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal", [(1, 8, 8, 4096, 128, True), (1, 4, 2, 1000, 64, True),
-                                                 (2, 2, 1, 777, 128, False), (1, 16, 16, 2048, 64, True)])
-def test_forward_key_split_matches_unsplit(cuda, B, Hq, Hkv, N, D, causal):
-    """On small grids the forward splits the key range of its heaviest query
-    blocks over two CTAs and merges the halves by their LSEs; without a
-    workspace it does not split. O and LSE must agree to rounding."""
+@pytest.mark.parametrize("N,D,causal", [(1024, 128, True), (1000, 64, True), (777, 128, False),
+                                         (2048, 64, False)])
+def test_small_grid_forward_matches_two_tile(cuda, N, D, causal):
+    """The forward launches one of two kernels by grid size: the two-tile one
+    (256 query rows per CTA) when B*Hq*ceil(N/256) fills the GPU, the
+    small-grid one (128 rows per CTA, 256-key steps) otherwise. The same heads
+    computed inside a large batch of heads and on their own take the two
+    paths; O and LSE must agree to rounding and both meet the oracle."""
     import _lib
     import fa_p100_ext
     g = torch.Generator(device="cuda").manual_seed(21)
-    mk = lambda h: torch.randn(B, h, N, D, device="cuda", generator=g).half()
-    q, k, v = mk(Hq), mk(Hkv), mk(Hkv)
-    lib = _lib.lib()
-    assert lib.fa_b200_forward_workspace_bytes(B, Hq, N, D, int(causal)) > 0
-    o_split, lse_split = fa_p100_ext.forward(q, k, v, causal)         # with the workspace
-    o = torch.empty_like(q)
-    lse = torch.empty(B, Hq, N, device="cuda")
-    st = lib.fa_b200_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                             lse.data_ptr(), B, Hq, Hkv, N, D, int(causal), 0,
-                             torch.cuda.current_stream().cuda_stream)   # no workspace: unsplit
-    _lib.check(st, "fa_b200_forward")
-    assert (o_split.float() - o.float()).abs().max().item() <= 2e-3
-    assert (lse_split - lse).abs().max().item() <= 1e-4
-    rq = orc.attention(q, k, v, causal, device=cuda)
-    assert orc.rel(o_split, rq) < 6e-2
+    H = 160                                   # 160 * ceil(N/256) >= 148: two-tile kernel
+    mk = lambda h: torch.randn(1, h, N, D, device="cuda", generator=g).half()
+    q, k, v = mk(H), mk(H), mk(H)
+    o_big, lse_big = fa_p100_ext.forward(q, k, v, causal)
+    qs, ks, vs = (t[:, :4].contiguous() for t in (q, k, v))   # 4 heads: small-grid kernel
+    o_small, lse_small = fa_p100_ext.forward(qs, ks, vs, causal)
+    assert (o_small.float() - o_big[:, :4].float()).abs().max().item() <= 2e-3
+    assert (lse_small - lse_big[:, :4]).abs().max().item() <= 1e-4
+    rq = orc.attention(qs, ks, vs, causal, device=cuda)
+    assert orc.rel(o_small, rq) < 6e-2
     assert _lib.device_error(0) == 0
+
+
+@pytest.mark.parametrize("H", [4, 160])            # small-grid and two-tile forward
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_causal_first_row_is_v0(cuda, H, D, dtype):
+    """A causal row 0 sees key 0 alone: its weight is exp(0) = 1 whatever the
+    score, so O[row 0] is V[0] to the last bit. This holds only if the row
+    maximum the softmax subtracts is exactly the row's largest score (P's
+    16-bit rounding then agrees with the fp32 row sum), so it pins the max
+    reduction over the masked S row."""
+    import fa_p100_ext
+    g = torch.Generator(device="cuda").manual_seed(3)
+    mk = lambda: (3 * torch.randn(1, H, 1024, D, device="cuda", generator=g)).to(dtype)
+    q, k, v = mk(), mk(), mk()
+    o, _ = fa_p100_ext.forward(q, k, v, True)
+    assert torch.equal(o[:, :, 0], v[:, :, 0])
