@@ -13,14 +13,15 @@
 //
 // fwd_kernel -- structure of one CTA (one CTA = 256 query rows of one
 // (batch, q-head)):
-//   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): two warpgroups,
-//               thread r of group h takes row r, columns 64h .. 64h+63
+//   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): each warp owns
+//               16 rows; lanes i and i+16 hold columns 0..63 and 64..127 of
+//               row i (TMEM shape 16x32bx2)
 //   warps 8-15  softmax for query tile 1 (rows m0+128 .. m0+255), the same way
 //   warp  16    TMEM allocation + the single thread that issues tcgen05.mma
 //   warp  17    the single thread that issues TMA loads
 // Two warps per SMSP share one tile's exponentials; the two halves of a row
-// exchange their partial maxima (and, at the end, row sums) through shared
-// memory under a per-tile mbarrier.
+// combine their partial maxima (and, at the end, row sums) with one shuffle,
+// so a tile's softmax warps meet only where P_t is handed to the MMA.
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
 // P_t (fp16 pairs, column 32 + c = keys 2c, 2c+1) is written back over
 // columns 32..95 of S_t: each half writes its 32 pair columns inside the 64 S
@@ -65,10 +66,9 @@ struct FwdCfg {
   static constexpr int STAGES = (D == 128) ? 4 : 8;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
-  static constexpr int OFF_X = OFF_RING + STAGES * KVBYTES;   // [tile][parity][half][row] floats
-  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 2 * 128 * 4;
-  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin, x[2]; then tmem addr + abort flag
-  static constexpr int NBAR = 1 + 2 * STAGES + 9;
+  static constexpr int OFF_BAR = OFF_RING + STAGES * KVBYTES;
+  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin; then tmem addr + abort flag
+  static constexpr int NBAR = 1 + 2 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 576;
@@ -123,8 +123,7 @@ __global__ void __maxnreg__(96)
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
   const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 16;
-  const uint32_t b_fin = b_o + 16, b_x = b_fin + 8;
-  float* xbuf = reinterpret_cast<float*>(sgen + C::OFF_X);
+  const uint32_t b_fin = b_o + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -154,7 +153,6 @@ __global__ void __maxnreg__(96)
     for (int t = 0; t < 2; ++t) {
       mbar_init(b_s + 8 * t, 1);
       mbar_init(b_p + 8 * t, 256);
-      mbar_init(b_x + 8 * t, 256);
       mbar_init(b_o + 8 * t, 1);
     }
     mbar_init(b_fin, 1);
@@ -285,19 +283,20 @@ __global__ void __maxnreg__(96)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax tile t, half hf
+    // ------------------------------------------------------------ softmax tile t
+    // Warp w of the tile takes the 16 rows at lanes 32*(w%4) + 16*((w>>2)&1) of
+    // its quadrant; lane i and lane i+16 share row i%16, holding its columns
+    // 0..63 (hf = 0) and 64..127 (hf = 1) through the 16x32bx2 TMEM shape, so
+    // the row's maximum and sum combine with one shuffle.
     const int t = warp >> 3;
-    const int hf = (warp >> 2) & 1;
-    const int r = threadIdx.x & 127;
+    const int hf = lane >> 4;
+    const int r = 32 * (warp & 3) + 16 * ((warp >> 2) & 1) + (lane & 15);
     const int row = m0 + 128 * t + r;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3) + 16 * ((warp >> 2) & 1)) << 16;
     const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
     const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
-    const uint32_t bx = b_x + 8 * t;
-    // partial row values of this tile: xbuf[((t * 2 + parity) * 2 + half) * 128 + r]
-    auto xslot = [&](int par, int half) { return xbuf + ((t * 2 + par) * 2 + half) * 128 + r; };
     const int nt = ntile[t];
-    const int c0 = 64 * hf;                  // this half's first column of S
+    const int c0 = 64 * hf;                  // this thread's first column of S
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -305,15 +304,10 @@ __global__ void __maxnreg__(96)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[2][32];
-      tmem_ld32(t_s + c0, sr[0]);
-      tmem_ld32(t_s + c0 + 32, sr[1]);
-      tmem_ld_wait_only();
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
-      float* s = reinterpret_cast<float*>(&sr[0][0]);
+      uint32_t sr[64];
+      tmem_ld16x2_x64(t_s, sr);
+      tmem_ld_wait(sr);
+      float* s = reinterpret_cast<float*>(sr);
       const int kb0 = j * 128;   // this step's first key
       const int col0 = kb0 + c0;
       const bool need_mask = (kb0 + 128 > p.n) || (p.causal && kb0 + 127 > m0 + 128 * t);
@@ -324,7 +318,7 @@ __global__ void __maxnreg__(96)
           if (col0 + c > lim) s[c] = -INFINITY;
       }
       // this half's max: 8 interleaved chains of three-input maxima over
-      // s[16..63], seeded with s[0..15], then a tree
+      // s[16..63], seeded with s[0..15], then a tree; the other half's by shuffle
       float mx8[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(s[c], s[c + 8]);
@@ -334,13 +328,7 @@ __global__ void __maxnreg__(96)
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
       const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
                               max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
-      // exchange with the other half of the row (buffer by step parity)
-      *xslot(j & 1, hf) = pmx;
-      mbar_arrive(bx);
-      ok = mbar_wait(bx, j & 1, ctl, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      const float mx = fmaxf(pmx, *xslot(j & 1, hf ^ 1));
+      const float mx = fmaxf(pmx, __shfl_xor_sync(0xffffffffu, pmx, 16));
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       // Rescale only when the running max grew by more than 2^8: P stays
       // below 256, and the final 1/l uses the same offset, so the result is
@@ -365,31 +353,27 @@ __global__ void __maxnreg__(96)
       // 32 pair columns go to COL_P + 32*hf .., inside the S columns it read
       const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
       uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
+      uint32_t w[32];
 #pragma unroll
-      for (int c32 = 0; c32 < 2; ++c32) {
-        uint32_t w[16];
-#pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const float2 x =
-              f32x2_split(fma_x2(f32x2(s[32 * c32 + 2 * h], s[32 * c32 + 2 * h + 1]), sl2, nm));
-          const float e0 = ex2(x.x), e1 = ex2(x.y);
-          lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
-          w[h] = pack2<BF>(e0, e1);
-        }
-        tmem_st16(t_s + C::COL_P + 32 * hf + 16 * c32, w);
+      for (int h = 0; h < 32; ++h) {
+        const float2 x = f32x2_split(fma_x2(f32x2(s[2 * h], s[2 * h + 1]), sl2, nm));
+        const float e0 = ex2(x.x), e1 = ex2(x.y);
+        lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
+        w[h] = pack2<BF>(e0, e1);
       }
+      tmem_st16x2_x32(t_s + C::COL_P, w);
       const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
       l += la.x + la.y;
-      if (rescale) {   // O_t *= alpha on this half's D/2 columns, before P_t is released
+      if (rescale) {   // O_t *= alpha on this thread's D/2 columns, before P_t is released
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           uint32_t orow[32];
-          const uint32_t a = t_o + hf * (D / 2) + 32 * c;
-          tmem_ld32(a, orow);
+          const uint32_t a = t_o + 64 * c;   // columns 64c + 32*hf ..
+          tmem_ld16x2_x32(a, orow);
           tmem_ld_wait(orow);
 #pragma unroll
           for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-          tmem_st32(a, orow);
+          tmem_st16x2_x32(a, orow);
         }
       }
       tmem_st_wait();
@@ -397,14 +381,10 @@ __global__ void __maxnreg__(96)
       mbar_arrive(b_p + 8 * t);
     }
     if (ok && nt > 0) {
-      // the row sum is the two halves' sums: one more exchange (phase nt)
-      *xslot(nt & 1, hf) = l;
-      mbar_arrive(bx);
-      ok = mbar_wait(bx, nt & 1, ctl, kErrTimeoutSoftmax) &&
-           mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);   // the row sum is the two halves' sums
+      ok = mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
-        l += *xslot(nt & 1, hf ^ 1);
         tc_fence_after();
         const float inv = 1.f / l;
         const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
@@ -414,9 +394,9 @@ __global__ void __maxnreg__(96)
         const uint32_t s_qt = t ? s_q1 : s_q0;
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
-          const int col = hf * (D / 2) + 32 * c;
+          const int col = 64 * c + 32 * hf;
           uint32_t orow[32];
-          tmem_ld32(t_o + col, orow);
+          tmem_ld16x2_x32(t_o + 64 * c, orow);
           tmem_ld_wait(orow);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
