@@ -440,8 +440,8 @@ namespace fab {
 // ---------------------------------------------------------------------------
 // Small-grid forward: one CTA per 128 query rows (twice the CTAs of the
 // two-tile kernel, for grids that would leave SMs idle), keys in steps of 256:
-//   warps 0-7   softmax: thread r of half h owns row r and keys 128h .. 128h+127
-//               of each step; the halves exchange row maxima and sums
+//   warps 0-7   softmax: each warp owns 16 rows; lanes i and i+16 hold keys
+//               0..127 and 128..255 of row i's step (TMEM shape 16x32bx2)
 //   warp  8     TMEM allocation + MMA issue;  warp 9  TMA loads
 // TMEM: S [0,256) fp32 | P [256,384) fp16 pairs of the step's 256 keys | O [384, 384+D).
 // P has columns of its own, so S of step j+1 (one N = 256 MMA) is issued as soon
@@ -460,10 +460,9 @@ struct FwdCfgS {
   static constexpr int KS = 2, VS = 1;          // K steps / V steps resident
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + QBYTES;
-  static constexpr int OFF_X = OFF_RING + (KS + VS) * KVBYTES;  // [parity][half][row] floats
-  static constexpr int OFF_BAR = OFF_X + 2 * 2 * 128 * 4;
-  // barriers: q, full[KS+VS], empty[KS+VS], s, sfree, p, pv, o, x
-  static constexpr int NBAR = 1 + 2 * (KS + VS) + 6;
+  static constexpr int OFF_BAR = OFF_RING + (KS + VS) * KVBYTES;
+  // barriers: q, full[KS+VS], empty[KS+VS], s, sfree, p, pv, o
+  static constexpr int NBAR = 1 + 2 * (KS + VS) + 5;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;   // window must start 1024-aligned
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 320;
@@ -513,8 +512,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * (C::KS + C::VS);
   const uint32_t b_s = b_empty + 8 * (C::KS + C::VS), b_sfree = b_s + 8, b_p = b_sfree + 8,
-                 b_pv = b_p + 8, b_o = b_pv + 8, b_x = b_o + 8;
-  float* xbuf = reinterpret_cast<float*>(smem_raw + C::OFF_X);
+                 b_pv = b_p + 8, b_o = b_pv + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -544,7 +542,6 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(b_p, 256);
     mbar_init(b_pv, 1);
     mbar_init(b_o, 1);
-    mbar_init(b_x, 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -644,15 +641,17 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    // thread r of half h owns row r and keys 128h .. 128h+127 of each step
-    const int h = warp >> 2;
-    const int r = threadIdx.x & 127;
+    // warp w owns the 16 rows at lanes 32*(w%4) + 16*(w>>2) of its quadrant;
+    // lane i and lane i+16 share row i%16, holding keys 0..127 (h = 0) and
+    // 128..255 (h = 1) of each step (TMEM shape 16x32bx2), so the row's
+    // maximum and sum combine with one shuffle
+    const int h = lane >> 4;
+    const int r = 32 * (warp & 3) + 16 * (warp >> 2) + (lane & 15);
     const int row = m0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem + C::COL_S + 128 * h + lane_off;
-    const uint32_t t_p = tmem + C::COL_P + 64 * h + lane_off;
-    const uint32_t t_o = tmem + C::COL_O + (D / 2) * h + lane_off;
-    auto xslot = [&](int par, int half) { return xbuf + (par * 2 + half) * 128 + r; };
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3) + 16 * (warp >> 2)) << 16;
+    const uint32_t t_s = tmem + C::COL_S + lane_off;
+    const uint32_t t_p = tmem + C::COL_P + lane_off;
+    const uint32_t t_o = tmem + C::COL_O + lane_off;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nstep; ++j) {
@@ -660,17 +659,12 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32 * c, sr[c]);
-      tmem_ld_wait_only();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+      uint32_t sr[128];
+      tmem_ld16x2_x128(t_s, sr);
+      tmem_ld_wait(sr);
       tc_fence_before();
       mbar_arrive(b_sfree);   // S(j+1) may overwrite the S columns now
-      float* s = reinterpret_cast<float*>(&sr[0][0]);
+      float* s = reinterpret_cast<float*>(sr);
       const int kb0 = j * C::BN + 128 * h;   // this thread's first key of the step
       const bool need_mask = (kb0 + 127 >= kend) || (p.causal && kb0 + 127 > m0);
       if (need_mask) {
@@ -688,13 +682,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
       const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
                               max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
-      // the other half of the row's maximum (buffer by step parity)
-      *xslot(j & 1, h) = pmx;
-      mbar_arrive(b_x);
-      ok = mbar_wait(b_x, j & 1, ctl, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      const float mx = fmaxf(pmx, *xslot(j & 1, h ^ 1));
+      const float mx = fmaxf(pmx, __shfl_xor_sync(0xffffffffu, pmx, 16));
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       // rescale only when the running max grew by more than 2^8 (P stays below
       // 256; the final 1/l uses the same offset); warp-wide because O is
@@ -731,46 +719,36 @@ __global__ void __launch_bounds__(320, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      if (rescale) {   // this half's D/2 columns of the O row
+      if (rescale) {   // this thread's D/2 columns of the O row
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           uint32_t orow[32];
-          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld16x2_x32(t_o + 64 * c, orow);   // columns 64c + 32h ..
           tmem_ld_wait(orow);
 #pragma unroll
           for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-          tmem_st32(t_o + 32 * c, orow);
+          tmem_st16x2_x32(t_o + 64 * c, orow);
         }
       }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = pk[16 * c + i];
-        tmem_st16(t_p + 16 * c, w);
-      }
+      tmem_st16x2_x64(t_p, pk);   // keys 128h.. as pairs: P columns 64h ..
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(b_p);
     }
     if (ok && nstep > 0) {
-      // the row sum is the two halves' sums: one more exchange (phase nstep)
-      *xslot(nstep & 1, h) = l;
-      mbar_arrive(b_x);
-      ok = mbar_wait(b_x, nstep & 1, ctl, kErrTimeoutSoftmax) &&
-           mbar_wait(b_o, 0, ctl, kErrTimeoutSoftmax);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);   // the row sum is the two halves' sums
+      ok = mbar_wait(b_o, 0, ctl, kErrTimeoutSoftmax);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
-        l += *xslot(nstep & 1, h ^ 1);
         tc_fence_after();
         const float inv = 1.f / l;
-        // O row rounded to 16 bits, staged as 64-column swizzled boxes over the
-        // Q tile (the last S has read it) and written by TMA stores below
+        // O row rounded to 16 bits, staged as 64-column swizzled boxes over
+        // the Q tile (the last S has read it) and written by TMA stores below
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
-          const int col = (D / 2) * h + 32 * c;
+          const int col = 64 * c + 32 * h;
           uint32_t orow[32];
-          tmem_ld32(t_o + 32 * c, orow);
+          tmem_ld16x2_x32(t_o + 64 * c, orow);
           tmem_ld_wait(orow);
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
