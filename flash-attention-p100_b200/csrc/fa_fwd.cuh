@@ -67,8 +67,8 @@ struct FwdCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
   static constexpr int OFF_BAR = OFF_RING + STAGES * KVBYTES;
-  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2], o[2], fin; then tmem addr + abort flag
-  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2][2], o[2], fin; then tmem addr + abort flag
+  static constexpr int NBAR = 1 + 2 * STAGES + 9;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 576;
@@ -96,14 +96,15 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_s, uint32_t
     mma_ss(d_tmem, sdesc_add(dq, off), sdesc_add(dk, off), idesc, kk > 0 ? 1u : 0u);
   }
 }
-// O[tmem] (+)= P (128 x 128 keys, fp16 pairs in TMEM) * V (128 keys x D, MN-major)
-template <int D, bool BF>
+// O[tmem] (+)= P (128 x keys [16*KK0, 16*KK1), fp16 pairs in TMEM) * V (those keys x D,
+// MN-major)
+template <int D, bool BF, int KK0 = 0, int KK1 = 8>
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_s,
                                          bool accumulate) {
   constexpr uint32_t idesc = idesc_f16(128, D, false, true, BF);
   const uint64_t dv = sdesc_sw128(v_s, 16384, 1024);
 #pragma unroll
-  for (int kk = 0; kk < 128 / 16; ++kk)
+  for (int kk = KK0; kk < KK1; ++kk)
     mma_ts(d_tmem, p_tmem + kk * 8, sdesc_add(dv, kk * 2048), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
 }
@@ -122,7 +123,8 @@ __global__ void __maxnreg__(96)
   const uint32_t s_ring = sbase + C::OFF_RING;
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
-  const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 16;
+  // b_p + 8*(2t + k): P_t's keys 0..63 (k = 0) / 64..127 (k = 1) are in TMEM
+  const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 32;
   const uint32_t b_fin = b_o + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -152,7 +154,8 @@ __global__ void __maxnreg__(96)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(b_s + 8 * t, 1);
-      mbar_init(b_p + 8 * t, 256);
+      mbar_init(b_p + 16 * t, 256);
+      mbar_init(b_p + 16 * t + 8, 256);
       mbar_init(b_o + 8 * t, 1);
     }
     mbar_init(b_fin, 1);
@@ -246,12 +249,20 @@ __global__ void __maxnreg__(96)
 #pragma unroll
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= ntile[t]) continue;
-          ok = mbar_wait(b_p + 8 * t, j & 1, ctl, kErrTimeoutMma);
+          // P_t in two halves of 64 keys: the first half's products run
+          // while the softmax computes the second half's exponentials
+          ok = mbar_wait(b_p + 16 * t, j & 1, ctl, kErrTimeoutMma);
           if (!ok) break;
           tc_fence_after();
-          issue_pv<D, BF>(tmem + (t ? C::COL_O1 : C::COL_O0),
-                      tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P, s_ring + slot_v * C::KVBYTES,
-                      j > 0);
+          issue_pv<D, BF, 0, 4>(tmem + (t ? C::COL_O1 : C::COL_O0),
+                                tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P,
+                                s_ring + slot_v * C::KVBYTES, j > 0);
+          ok = mbar_wait(b_p + 16 * t + 8, j & 1, ctl, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv<D, BF, 4, 8>(tmem + (t ? C::COL_O1 : C::COL_O0),
+                                tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P,
+                                s_ring + slot_v * C::KVBYTES, true);
           if (j + 1 < ntile[t]) {
             if (!have_k) {
               ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
@@ -286,8 +297,10 @@ __global__ void __maxnreg__(96)
     // ------------------------------------------------------------ softmax tile t
     // Warp w of the tile takes the 16 rows at lanes 32*(w%4) + 16*((w>>2)&1) of
     // its quadrant; lane i and lane i+16 share row i%16, holding its columns
-    // 0..63 (hf = 0) and 64..127 (hf = 1) through the 16x32bx2 TMEM shape, so
-    // the row's maximum and sum combine with one shuffle.
+    // 32hf..32hf+31 and 64+32hf..64+32hf+31 (hf = 0, 1) through the 16x32bx2
+    // TMEM shape, so the row's maximum and sum combine with one shuffle. P goes
+    // back in two halves (keys 0..63, then 64..127), each released on its own
+    // barrier.
     const int t = warp >> 3;
     const int hf = lane >> 4;
     const int r = 32 * (warp & 3) + 16 * ((warp >> 2) & 1) + (lane & 15);
@@ -296,7 +309,6 @@ __global__ void __maxnreg__(96)
     const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
     const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
     const int nt = ntile[t];
-    const int c0 = 64 * hf;                  // this thread's first column of S
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
@@ -304,18 +316,20 @@ __global__ void __maxnreg__(96)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      // s[c] is key 32*hf + c (c < 32) or 64 + 32*hf + (c - 32) of the block
       uint32_t sr[64];
-      tmem_ld16x2_x64(t_s, sr);
+      tmem_ld16x2_x32(t_s, reinterpret_cast<uint32_t(&)[32]>(sr[0]));
+      tmem_ld16x2_x32(t_s + 64, reinterpret_cast<uint32_t(&)[32]>(sr[32]));
       tmem_ld_wait(sr);
       float* s = reinterpret_cast<float*>(sr);
       const int kb0 = j * 128;   // this step's first key
-      const int col0 = kb0 + c0;
+      const int col0 = kb0 + 32 * hf;
       const bool need_mask = (kb0 + 128 > p.n) || (p.causal && kb0 + 127 > m0 + 128 * t);
       if (need_mask) {
         const int lim = p.causal ? min(p.n - 1, row) : (p.n - 1);
 #pragma unroll
         for (int c = 0; c < 64; ++c)
-          if (col0 + c > lim) s[c] = -INFINITY;
+          if (col0 + c + 32 * (c / 32) > lim) s[c] = -INFINITY;
       }
       // this half's max: 8 interleaved chains of three-input maxima over
       // s[16..63], seeded with s[0..15], then a tree; the other half's by shuffle
@@ -349,21 +363,21 @@ __global__ void __maxnreg__(96)
         }
       }
       // P = 2^(s*scale*log2e - m) on column pairs: one packed FMA and one
-      // packed add (row sum, two chains of pairs) per two columns; this half's
-      // 32 pair columns go to COL_P + 32*hf .., inside the S columns it read
+      // packed add (row sum, two chains of pairs) per two columns. Pair
+      // column COL_P + k/2 holds keys k, k+1: the first 16 of this thread's
+      // pairs go to COL_P + 16*hf .. (keys 0..63 between the two threads),
+      // the rest to COL_P + 32 + 16*hf .., all inside S columns already read
       const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
       uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
-      uint32_t w[32];
+      uint32_t w[16];
 #pragma unroll
-      for (int h = 0; h < 32; ++h) {
+      for (int h = 0; h < 16; ++h) {
         const float2 x = f32x2_split(fma_x2(f32x2(s[2 * h], s[2 * h + 1]), sl2, nm));
         const float e0 = ex2(x.x), e1 = ex2(x.y);
         lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
         w[h] = pack2<BF>(e0, e1);
       }
-      tmem_st16x2_x32(t_s + C::COL_P, w);
-      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
-      l += la.x + la.y;
+      tmem_st16x2_x16(t_s + C::COL_P, w);
       if (rescale) {   // O_t *= alpha on this thread's D/2 columns, before P_t is released
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
@@ -378,7 +392,20 @@ __global__ void __maxnreg__(96)
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(b_p + 8 * t);
+      mbar_arrive(b_p + 16 * t);   // keys 0..63 of P_t (and O_t rescaled)
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float2 x = f32x2_split(fma_x2(f32x2(s[32 + 2 * h], s[33 + 2 * h]), sl2, nm));
+        const float e0 = ex2(x.x), e1 = ex2(x.y);
+        lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
+        w[h] = pack2<BF>(e0, e1);
+      }
+      tmem_st16x2_x16(t_s + C::COL_P + 32, w);
+      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
+      l += la.x + la.y;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(b_p + 16 * t + 8);   // keys 64..127
     }
     if (ok && nt > 0) {
       l += __shfl_xor_sync(0xffffffffu, l, 16);   // the row sum is the two halves' sums
