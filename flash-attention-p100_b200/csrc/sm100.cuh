@@ -505,39 +505,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                "r"(d)
                : "memory");
 }
-// Four fp32 atomic adds to 16 consecutive bytes of global memory (performed at L2).
+// 2^x on the MUFU unit (approximate, flush-to-zero; 2^-inf = 0).
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA/ALU pipes, to take part of the exponentials off the MUFU unit
-// (one ex2 occupies it for 8 cycles per warp; softmax-heavy loops saturate it).
-// Cody-Waite style reduction x = n + f: adding 1.5*2^23 rounds x to the
-// nearest integer n inside the low mantissa bits of t, f = x - n is in
-// [-0.5, 0.5], 2^f comes from a degree-4 polynomial fitted for this library by
-// iteratively reweighted least squares on [-0.5, 0.5] (max relative error
-// 2.7e-6, below fp16's 4.9e-4 half-ulp), and 2^n is added into the exponent
-// field with one integer multiply-add (the low 9 bits of t hold n mod 512).
-// x is clamped to >= -125 so the exponent never underflows; results below
-// 2^-125 are far under fp16's range and every caller masks with 0 explicitly.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  float p = fmaf(f, 0.009570376f, 0.055918723f);
-  p = fmaf(p, f, 0.24024746f);
-  p = fmaf(p, f, 0.69312167f);
-  p = fmaf(p, f, 0.99999928f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-// Mixed exponential for fully unrolled column loops (c is then a constant and
-// the choice folds away): columns with c % 3 == 0 use the polynomial, the
-// rest the MUFU ex2, which roughly balances the two pipes.
-__device__ __forceinline__ float exp2_mixed(float x, int c) {
-  return (c % 3 == 0) ? exp2_poly(x) : ex2(x);
 }
 
 // Byte offset of 16-byte piece `c` (0..D/8-1) of row `r` in a swizzled tile of
