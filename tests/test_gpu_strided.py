@@ -13,9 +13,13 @@ import fa_p100_ext
 pytestmark = pytest.mark.gpu
 
 CASES = [  # B, Hq, Hkv, N, D, causal
+    # B*Hq*ceil(N/256) below the SM count: the small-grid forward
     (2, 4, 2, 300, 64, True),
     (1, 8, 8, 1000, 128, False),
     (2, 6, 1, 513, 128, True),
+    # enough 256-row blocks to fill the GPU: the two-tile forward
+    (2, 40, 8, 1000, 128, True),
+    (1, 80, 80, 600, 64, False),
 ]
 
 
