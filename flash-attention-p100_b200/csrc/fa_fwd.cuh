@@ -14,8 +14,8 @@
 // fwd_kernel -- structure of one CTA (one CTA = 256 query rows of one
 // (batch, q-head)):
 //   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): each warp owns
-//               16 rows; lanes i and i+16 hold columns 0..63 and 64..127 of
-//               row i (TMEM shape 16x32bx2)
+//               16 rows; lanes i and i+16 hold columns {0..31, 64..95} and
+//               {32..63, 96..127} of row i (TMEM shape 16x32bx2)
 //   warps 8-15  softmax for query tile 1 (rows m0+128 .. m0+255), the same way
 //   warp  16    TMEM allocation + the single thread that issues tcgen05.mma
 //   warp  17    the single thread that issues TMA loads
@@ -24,8 +24,8 @@
 // so a tile's softmax warps meet only where P_t is handed to the MMA.
 // TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
 // P_t (fp16 pairs, column 32 + c = keys 2c, 2c+1) is written back over
-// columns 32..95 of S_t: each half writes its 32 pair columns inside the 64 S
-// columns it has already read into registers. O_t += P_t V_j reads P_t from
+// columns 32..95 of S_t, inside S columns its warp has already read into
+// registers, in two pieces (keys 0..63, then 64..127). O_t += P_t V_j reads P_t from
 // TMEM, so P never touches shared memory, and V is the MMA's only shared operand.
 // Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate).
 //
@@ -488,8 +488,8 @@ struct FwdCfgS {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_RING = OFF_Q + QBYTES;
   static constexpr int OFF_BAR = OFF_RING + (KS + VS) * KVBYTES;
-  // barriers: q, full[KS+VS], empty[KS+VS], s, sfree, p, pv, o
-  static constexpr int NBAR = 1 + 2 * (KS + VS) + 5;
+  // barriers: q, full[KS+VS], empty[KS+VS], s, sfree, p[2], pv, o
+  static constexpr int NBAR = 1 + 2 * (KS + VS) + 6;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16;   // window must start 1024-aligned
   static_assert(SMEM <= 232448, "shared memory over the per-block limit");
   static constexpr int THREADS = 320;
@@ -513,15 +513,16 @@ __device__ __forceinline__ void issue_qk256(uint32_t d_tmem, uint32_t q_s, uint3
     mma_ss(d_tmem, sdesc_add(dq, (kk >> 2) * 16384 + (kk & 3) * 32),
            sdesc_add(dk, (kk >> 2) * C::CHUNK + (kk & 3) * 32), idesc, kk > 0 ? 1u : 0u);
 }
-// O[tmem] (+)= P (128 x 256 keys, fp16 pairs in TMEM) * V_step (256 keys x D, MN-major)
-template <int D, bool BF>
+// O[tmem] (+)= P (128 x keys [16*KK0, 16*KK1) of the step, fp16 pairs in TMEM) * V_step
+// (those keys x D, MN-major)
+template <int D, bool BF, int KK0, int KK1>
 __device__ __forceinline__ void issue_pv256(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_s,
                                          bool accumulate) {
   using C = FwdCfgS<D>;
   constexpr uint32_t idesc = idesc_f16(128, D, false, true, BF);
   const uint64_t dv = sdesc_sw128(v_s, C::CHUNK, 1024);
 #pragma unroll
-  for (int kk = 0; kk < 256 / 16; ++kk)
+  for (int kk = KK0; kk < KK1; ++kk)
     mma_ts(d_tmem, p_tmem + kk * 8, sdesc_add(dv, kk * 2048), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
 }
@@ -538,8 +539,9 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t s_q = sbase + C::OFF_Q, s_ring = sbase + C::OFF_RING;
   const uint32_t b_q = sbase + C::OFF_BAR;
   const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * (C::KS + C::VS);
+  // b_p + 8k: keys 128k .. 128k+127 of the step's P are in TMEM
   const uint32_t b_s = b_empty + 8 * (C::KS + C::VS), b_sfree = b_s + 8, b_p = b_sfree + 8,
-                 b_pv = b_p + 8, b_o = b_pv + 8;
+                 b_pv = b_p + 16, b_o = b_pv + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + C::OFF_BAR + C::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -567,6 +569,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(b_s, 1);
     mbar_init(b_sfree, 256);
     mbar_init(b_p, 256);
+    mbar_init(b_p + 8, 256);
     mbar_init(b_pv, 1);
     mbar_init(b_o, 1);
     *abort_flag = 0;
@@ -650,12 +653,19 @@ __global__ void __launch_bounds__(320, 1)
           mma_commit(b_s);
           mma_commit(b_empty + 8 * k_slot(j + 1));
         }
-        // O += P(j) V_j
+        // O += P(j) V_j, in two halves of 128 keys: the first half's products
+        // run while the softmax computes the second half's exponentials
         ok = mbar_wait(b_full + 8 * v_slot(j), v_ph(j), ctl, kErrTimeoutMma) &&
              mbar_wait(b_p, j & 1, ctl, kErrTimeoutMma);
         if (!ok) break;
         tc_fence_after();
-        issue_pv256<D, BF>(tmem + C::COL_O, tmem + C::COL_P, s_ring + v_slot(j) * C::KVBYTES, j > 0);
+        issue_pv256<D, BF, 0, 8>(tmem + C::COL_O, tmem + C::COL_P, s_ring + v_slot(j) * C::KVBYTES,
+                                 j > 0);
+        ok = mbar_wait(b_p + 8, j & 1, ctl, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv256<D, BF, 8, 16>(tmem + C::COL_O, tmem + C::COL_P,
+                                  s_ring + v_slot(j) * C::KVBYTES, true);
         mma_commit(b_pv);
         mma_commit(b_empty + 8 * v_slot(j));
         if (j + 1 == nstep) mma_commit(b_o);
@@ -669,9 +679,10 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // ------------------------------------------------------------ softmax
     // warp w owns the 16 rows at lanes 32*(w%4) + 16*(w>>2) of its quadrant;
-    // lane i and lane i+16 share row i%16, holding keys 0..127 (h = 0) and
-    // 128..255 (h = 1) of each step (TMEM shape 16x32bx2), so the row's
-    // maximum and sum combine with one shuffle
+    // lane i and lane i+16 share row i%16, holding keys 64h..64h+63 and
+    // 128+64h..128+64h+63 of each step (h = 0, 1; TMEM shape 16x32bx2), so the
+    // row's maximum and sum combine with one shuffle, and P goes back in two
+    // halves of 128 keys, each released on its own barrier
     const int h = lane >> 4;
     const int r = 32 * (warp & 3) + 16 * (warp >> 2) + (lane & 15);
     const int row = m0 + r;
@@ -686,19 +697,21 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      // s[c] is key 64h + c (c < 64) or 128 + 64h + (c - 64) of the step
       uint32_t sr[128];
-      tmem_ld16x2_x128(t_s, sr);
+      tmem_ld16x2_x64(t_s, reinterpret_cast<uint32_t(&)[64]>(sr[0]));
+      tmem_ld16x2_x64(t_s + 128, reinterpret_cast<uint32_t(&)[64]>(sr[64]));
       tmem_ld_wait(sr);
       tc_fence_before();
       mbar_arrive(b_sfree);   // S(j+1) may overwrite the S columns now
       float* s = reinterpret_cast<float*>(sr);
-      const int kb0 = j * C::BN + 128 * h;   // this thread's first key of the step
-      const bool need_mask = (kb0 + 127 >= kend) || (p.causal && kb0 + 127 > m0);
+      const int kb0 = j * C::BN + 64 * h;   // this thread's first key of the step
+      const bool need_mask = (j * C::BN + C::BN > kend) || (p.causal && j * C::BN + C::BN - 1 > m0);
       if (need_mask) {
         const int lim = p.causal ? min(kend - 1, row) : (kend - 1);
 #pragma unroll
         for (int c = 0; c < 128; ++c)
-          if (kb0 + c > lim) s[c] = -INFINITY;
+          if (kb0 + c + 64 * (c / 64) > lim) s[c] = -INFINITY;
       }
       float mx8[8];   // as in fwd_kernel, over this half's 128 keys
 #pragma unroll
@@ -727,18 +740,22 @@ __global__ void __launch_bounds__(320, 1)
           m_used = m_new;
         }
       }
+      // P in pair columns (column c holds keys 2c, 2c+1 of the step): this
+      // thread's first 32 pairs go to columns 32h .. (keys 0..127 between the
+      // two threads of the row), the other 32 to 64 + 32h ..
       const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
       uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
-      uint32_t pk[64];
+      uint32_t pk[32];
+      auto exps32 = [&](int c0) {
 #pragma unroll
-      for (int q2 = 0; q2 < 64; ++q2) {
-        const float2 x = f32x2_split(fma_x2(f32x2(s[2 * q2], s[2 * q2 + 1]), sl2, nm));
-        const float e0 = ex2(x.x), e1 = ex2(x.y);
-        lp[q2 & 1] = add_x2(lp[q2 & 1], f32x2(e0, e1));
-        pk[q2] = pack2<BF>(e0, e1);
-      }
-      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
-      l += la.x + la.y;
+        for (int q2 = 0; q2 < 32; ++q2) {
+          const float2 x = f32x2_split(fma_x2(f32x2(s[c0 + 2 * q2], s[c0 + 2 * q2 + 1]), sl2, nm));
+          const float e0 = ex2(x.x), e1 = ex2(x.y);
+          lp[q2 & 1] = add_x2(lp[q2 & 1], f32x2(e0, e1));
+          pk[q2] = pack2<BF>(e0, e1);
+        }
+      };
+      exps32(0);
       // O += P(j-1) V must be complete before P and O are rewritten
       if (j > 0) {
         ok = mbar_wait(b_pv, (j - 1) & 1, ctl, kErrTimeoutSoftmax);
@@ -757,10 +774,17 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st16x2_x32(t_o + 64 * c, orow);
         }
       }
-      tmem_st16x2_x64(t_p, pk);   // keys 128h.. as pairs: P columns 64h ..
+      tmem_st16x2_x32(t_p, pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(b_p);
+      mbar_arrive(b_p);       // keys 0..127 of P(j) (and O rescaled)
+      exps32(64);
+      tmem_st16x2_x32(t_p + 64, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(b_p + 8);   // keys 128..255
+      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
+      l += la.x + la.y;
     }
     if (ok && nstep > 0) {
       l += __shfl_xor_sync(0xffffffffu, l, 16);   // the row sum is the two halves' sums
