@@ -1,26 +1,39 @@
 #!/usr/bin/env python
 """Attention fwd+bwd benchmark (BASELINE.json metric: attention fwd+bwd TFLOPS per
-GPU and % of the fp16 tensor peak).
+GPU and % of the fp16 tensor peak; Qwen3-0.6B-shaped step ms).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload C2|C1|C3a|C3b|north_star]
+                    [--workload C3a|...] [--ring]
 
 One step = one forward + one backward of the attention hot path over one batch
-of seeded synthetic fp16 inputs (i.i.d. N(0,1), as BASELINE.json's configs say).
-The default workload is configs[1] (C2: B=1, Hq=Hkv=8, N=4096, D=128, causal).
+of seeded synthetic fp16 inputs (i.i.d. N(0,1), x0.5 for config 3, as
+BASELINE.json's configs say). The default workload is C3a causal (B=4, Hq=32,
+Hkv=8, N=3000, D=128): the largest single-GPU attention configuration.
 
-Our arm (--impl ours):
-  value   whole-job TFLOPS with inputs resident in HBM, through the C ABI
-          (fa_b200_forward_strided + fa_b200_backward_stages), L2 flushed (256 MiB
-          write) between steps outside the timed events;
-  e2e     the same metric through the public API (fa_p100.flash_attn + autograd
-          backward) with q, k, v, dO copied from pinned host memory and dq, dk,
-          dv copied back inside the timed region;
-  roofline the dominant kernel's algorithmic FLOPs / its CUDA-event time;
+Our arm (--impl ours), one JSON line from rank 0:
+  value     whole-job TFLOPS with inputs resident in HBM, through the C ABI
+            (fa_b200_forward_strided + fa_b200_backward_stages), L2 flushed
+            (256 MiB write) between steps, outside the timed events;
+  e2e       the same metric through the public API (fa_p100.flash_attn +
+            autograd backward) with q, k, v, dO copied from pinned host memory
+            and dq, dk, dv copied back inside the timed region;
+  roofline  the dominant kernel's algorithmic FLOPs (or bytes) / its CUDA-event
+            time, against MEASURED_PEAKS.json;
+  sdpa      torch fp16 scaled_dot_product_attention fwd+bwd on the same inputs,
+            same L2 flush and CUDA events (the reference's own comparison,
+            bench_train.py:24-58);
+  north_star, c1, c2, c3a_noncausal   the same measurement (ours and SDPA) at
+            (1,32,8192,128) causal, C1, C2 and C3a non-causal (N=1 only);
+  qwen3_0p6b_step_ms   BASELINE config 4 through the HF registration vs SDPA;
   cpu_baseline  the reference's CPU path (torch fp32 eager attention, restated
-          in oracle/) on a bounded sample, rank 0 at N=1 only.
-Multi-GPU (torchrun): heads are sharded, each rank runs its own full workload
-with no collective on the data path (weak scaling); time = max over ranks.
+            in oracle/) on one (batch, kv-head) group of the workload,
+            extrapolated to the whole workload by FLOPs (rank 0, N=1).
+Multi-GPU (torchrun, N>1): `value` is N data-parallel replicas -- every rank
+runs its own C3a batch, no collective on the data path (weak scaling), time =
+max over ranks; `ring_c5` is BASELINE config 5 (B=1, Hq=32, Hkv=8, N=131072)
+zigzag-sharded over the N ranks with ring context parallelism (NCCL
+send/recv of K/V and the travelling dK/dV accumulators, strong scaling), its
+efficiency measured against the same problem on one GPU in the same job.
 
 The reference arm (--impl reference) times the reference's CPU implementation
 of the path (fa_p100.reference, restated in oracle/attention_oracle.py) on the
@@ -28,7 +41,6 @@ host cores, rank 0 only.
 """
 import argparse
 import json
-import math
 import os
 import statistics
 import sys
@@ -49,18 +61,30 @@ WORKLOADS = {
     # name: (B, Hq, Hkv, N, D, causal, input scale)
     "C1": (1, 16, 16, 2048, 64, True, 1.0),
     "C2": (1, 8, 8, 4096, 128, True, 1.0),
-    "C3a": (4, 32, 8, 3000, 128, False, 0.5),
-    "C3b": (2, 16, 1, 1537, 64, False, 0.5),
+    "C3a": (4, 32, 8, 3000, 128, True, 0.5),
+    "C3a_noncausal": (4, 32, 8, 3000, 128, False, 0.5),
+    "C3b": (2, 16, 1, 1537, 64, True, 0.5),
+    "C3b_noncausal": (2, 16, 1, 1537, 64, False, 0.5),
     "north_star": (1, 32, 32, 8192, 128, True, 1.0),
+    "qwen3_layer": (1, 16, 8, 8192, 128, True, 1.0),
     "C5": (1, 32, 8, 131072, 128, True, 1.0),
 }
+# measured beside the headline at N=1 (key in the JSON line: workload)
+SIDE_WORKLOADS = {"north_star": "north_star", "c1": "C1", "c2": "C2",
+                  "c3a_noncausal": "C3a_noncausal", "qwen3_layer": "qwen3_layer"}
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
+FLOP_CONVENTION = "fwd 4*B*Hq*D*pairs (causal pairs N(N+1)/2), fwd+bwd 3.5x"
 
 
 def flops_fwd(B, Hq, N, D, causal):
     pairs = N * (N + 1) / 2 if causal else float(N) * N
     return 4.0 * B * Hq * D * pairs
+
+
+def step_flops(workload):
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS[workload]
+    return 3.5 * flops_fwd(B, Hq, N, D, causal)
 
 
 def load_peak():
@@ -91,7 +115,7 @@ class ClockSampler:
         "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_indices, period_s=0.01):
+    def __init__(self, device_indices, period_s=0.005):
         self.period = period_s
         self.samples = []
         self.max_mhz = None
@@ -186,9 +210,11 @@ def cpu_sample_shape(workload):
     return 1, Hq // Hkv, 1, N, D, causal, sc
 
 
-def cpu_step_tflops(workload, steps, warmup, min_seconds=0.0):
-    """Median TFLOPS of the CPU reference step over `steps` timed calls (more
-    calls, up to 200, until `min_seconds` of CPU work have been timed)."""
+def cpu_step(workload, steps, warmup, min_seconds=0.0):
+    """The CPU reference step on one (batch, kv-head) group of `workload`.
+    Returns (TFLOPS, extrapolated whole-workload ms per step, threads, sample
+    description); the slice's TFLOPS stands for the whole workload's, whose
+    time is extrapolated by FLOPs."""
     from oracle import attention_oracle as orc
     torch.set_num_threads(os.cpu_count() or 1)
     B, Hq, Hkv, N, D, causal, sc = cpu_sample_shape(workload)
@@ -201,23 +227,27 @@ def cpu_step_tflops(workload, steps, warmup, min_seconds=0.0):
         orc.reference_step(q, k, v, do, causal)
         times.append(time.perf_counter() - t0)
     fl = 3.5 * flops_fwd(B, Hq, N, D, causal)
-    ms = statistics.median(times) * 1e3
-    sample = (f"{B}x{Hq}q/{Hkv}kv heads of {workload}, N={N}, D={D}, causal={causal}: "
-              f"torch fp32 eager fwd+bwd (fa_p100.reference formula) on the host")
-    return fl / (ms * 1e-3) / 1e12, ms, torch.get_num_threads(), sample
+    ms_slice = statistics.median(times) * 1e3
+    tflops = fl / (ms_slice * 1e-3) / 1e12
+    ms_full = ms_slice * step_flops(workload) / fl
+    sample = (f"one (batch, kv-head) group of {workload} ({Hq} q heads / 1 kv head, N={N}, D={D}, "
+              f"causal={causal}), median of {len(times)} steps of {ms_slice:.1f} ms: torch fp32 "
+              f"eager fwd+bwd (fa_p100.reference formula) on the host; whole-workload time "
+              f"extrapolated by FLOPs")
+    return tflops, ms_full, torch.get_num_threads(), sample
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
-    value, ms, cores, sample = cpu_step_tflops(args.workload, args.steps, args.warmup)
+    value, ms, cores, sample = cpu_step(args.workload, args.steps, args.warmup)
     B, Hq, Hkv, N, D, causal, _ = WORKLOADS[args.workload]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
-                   "causal": causal, "sample": sample},
+                   "causal": causal, "sample": sample, "flop_convention": FLOP_CONVENTION},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -257,6 +287,169 @@ def kernel_work(name, B, Hq, Hkv, N, D, causal):
     if name == "bwd_dq":
         return 0.5 * ff, "TFLOP/s", "tensor"
     return 2.0 * B * Hq * N * D * 2 + 2 * B * Hq * N * 4 + B * Hq * N * D * 4, "GB/s", "hbm"
+
+
+def seeded_device_inputs(workload, dev, seed):
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[workload]
+    gen = torch.Generator(device=dev).manual_seed(seed)
+
+    def rnd(h):
+        return (torch.randn(B, h, N, D, device=dev, generator=gen) * sc).half()
+
+    return rnd(Hq), rnd(Hkv), rnd(Hkv), rnd(Hq)
+
+
+def split_group(B, Hq, Hkv, N, dev):
+    """Whether the fused backward splits a GQA group (it then adds the dK/dV
+    accumulator conversion launch); the library's own rule."""
+    return (Hq > Hkv and B * Hkv * ((N + 127) // 128)
+            < 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+
+
+def time_kernels(lib, dev, workload, q, k, v, do, steps, warmup, flush, deterministic=False,
+                 clocks=None, world=1):
+    """Our kernels on resident inputs through the C ABI: per step one forward,
+    the row-sum preprocess and the fused backward (or, deterministic, the dK/dV
+    and dQ kernels), CUDA events on the launching stream around each launch, L2
+    flushed between steps outside the events. Returns (ms per step, {kernel: ms})."""
+    import _lib
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS[workload]
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, N, device=dev)
+    kernels, stages, dq_fp32 = PATHS["deterministic" if deterministic else "fused"]
+    dq = torch.empty(q.shape, device=dev, dtype=torch.float32 if dq_fp32 else torch.float16)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
+    ws = torch.empty(ws_bytes // 4, device=dev)
+    sq, skv = _lib.strides_of(q), _lib.strides_of(k)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    step_ev = []
+
+    def step(record):
+        nk = len(kernels)
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] if record else None
+        if record:
+            marks[0].record(stream)
+        st = lib.fa_b200_forward_strided(q.data_ptr(), sq, k.data_ptr(), skv, v.data_ptr(), skv,
+                                         o.data_ptr(), sq, lse.data_ptr(), B, Hq, Hkv, N, D,
+                                         _lib.DTYPE_FP16, int(causal), 0, sp)
+        _lib.check(st, "fa_b200_forward_strided")
+        for i, mask in enumerate(stages):
+            if record:
+                marks[i + 1].record(stream)
+            st = lib.fa_b200_backward_stages(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), o.data_ptr(),
+                lse.data_ptr(), dq.data_ptr(), dq_fp32, dk.data_ptr(), dv.data_ptr(),
+                ws.data_ptr(), ws_bytes, B, Hq, Hkv, N, D, int(causal), mask, sp)
+            _lib.check(st, "fa_b200_backward_stages")
+        if record:
+            marks[nk].record(stream)
+            step_ev.append(marks)
+
+    for _ in range(warmup):
+        flush.fill_(1.0)
+        step(False)
+    torch.cuda.synchronize(dev)
+    if _lib.device_error(dev.index) != 0:
+        raise RuntimeError(f"device error word set during the {workload} warm-up")
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        for _ in range(steps):
+            flush.fill_(1.0)   # L2 flush, outside the step's events
+            step(True)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    if _lib.device_error(dev.index) != 0:
+        raise RuntimeError(f"device error word set during the {workload} timed steps")
+    per_kernel = {n: 0.0 for n in kernels}
+    total = 0.0
+    for m in step_ev:
+        for i, n in enumerate(kernels):
+            per_kernel[n] += m[i].elapsed_time(m[i + 1])
+        total += m[0].elapsed_time(m[len(kernels)])
+    return total / steps, {n: t / steps for n, t in per_kernel.items()}
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def time_sdpa(dev, workload, q, k, v, do, steps, warmup, flush):
+    """torch fp16 scaled_dot_product_attention fwd+bwd (torch's default SDPA
+    dispatch, GQA through enable_gqa) on the same inputs, L2 flushed between
+    steps outside the events. Returns ms per step."""
+    import torch.nn.functional as F
+    causal = WORKLOADS[workload][5]
+    gqa = q.size(1) != k.size(1)
+    qs, ks, vs = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+
+    def step():
+        for t in (qs, ks, vs):
+            t.grad = None
+        out = F.scaled_dot_product_attention(qs, ks, vs, is_causal=causal, enable_gqa=gqa)
+        out.backward(do)
+
+    for _ in range(warmup):
+        flush.fill_(1.0)
+        step()
+    torch.cuda.synchronize(dev)
+    total = 0.0
+    for _ in range(steps):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    del qs, ks, vs
+    return total / steps
+
+
+def kernel_report(workload, per_kernel, peak_tf, peak_gbs, peak_src):
+    """Per-kernel achieved rates and the roofline of the dominant kernel."""
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS[workload]
+    kernels = {}
+    for n, ms in per_kernel.items():
+        w, u, _ = kernel_work(n, B, Hq, Hkv, N, D, causal)
+        kernels[n] = {"ms": ms, "achieved": w / (ms * 1e-3) / (1e12 if u == "TFLOP/s" else 1e9),
+                      "unit": u}
+    dom = max(per_kernel, key=per_kernel.get)
+    work, unit, bound = kernel_work(dom, B, Hq, Hkv, N, D, causal)
+    achieved = kernels[dom]["achieved"]
+    peak = peak_tf if unit == "TFLOP/s" else peak_gbs
+    roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak, "traffic": load_traffic(workload).get(dom),
+                "algorithmic_per_launch": work, "peak_source": peak_src}
+    return kernels, roofline
+
+
+def side_measurement(lib, dev, workload, steps, warmup, flush, peaks, seed=4321):
+    """Our kernels and SDPA at one more workload: value, % of peak, per-kernel
+    rates, roofline and the SDPA comparison."""
+    peak_tf, peak_gbs, peak_src = peaks
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[workload]
+    q, k, v, do = seeded_device_inputs(workload, dev, seed)
+    ms, per_kernel = time_kernels(lib, dev, workload, q, k, v, do, steps, warmup, flush)
+    sd_ms = time_sdpa(dev, workload, q, k, v, do, steps, warmup, flush)
+    fl = step_flops(workload)
+    value = fl / (ms * 1e-3) / 1e12
+    kernels, roofline = kernel_report(workload, per_kernel, peak_tf, peak_gbs, peak_src)
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    return {"workload": workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D, "causal": causal,
+            "value": value, "unit": UNIT, "ms_per_step": ms,
+            "pct_of_peak": 100.0 * value / peak_tf, "kernels": kernels, "roofline": roofline,
+            "sdpa": {"value": fl / (sd_ms * 1e-3) / 1e12, "ms_per_step": sd_ms},
+            "vs_sdpa": sd_ms / ms}
 
 
 def qwen3_step_ms(dev, attn, steps, warmup, seq=8192):
@@ -313,6 +506,8 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lib = _lib.lib()
+    peaks = load_peak()
+    peak_tf, peak_gbs, peak_src = peaks
     B, Hq, Hkv, N, D, causal, sc = WORKLOADS[args.workload]
     gen = torch.Generator(device="cpu").manual_seed(1234 + rank)
 
@@ -321,79 +516,20 @@ def run_ours(args, world, rank, local):
 
     q_h, k_h, v_h, do_h = rnd(Hq), rnd(Hkv), rnd(Hkv), rnd(Hq)
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
-    o = torch.empty_like(q)
-    lse = torch.empty(B, Hq, N, device=dev)
-    KERNELS, STAGES, dq_fp32 = PATHS["deterministic" if args.deterministic else "fused"]
-    dq = torch.empty(q.shape, device=dev, dtype=torch.float32 if dq_fp32 else torch.float16)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
-    ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
-    ws = torch.empty(ws_bytes // 4, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
-    sq, skv = _lib.strides_of(q), _lib.strides_of(k)
-    stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
-    ev = {n: [] for n in KERNELS}
-    step_ev = []
+    n_kernels = 4 if args.deterministic else 3
+    split = not args.deterministic and split_group(B, Hq, Hkv, N, dev)
 
-    def bwd_stage(mask):
-        return lib.fa_b200_backward_stages(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), o.data_ptr(),
-            lse.data_ptr(), dq.data_ptr(), dq_fp32, dk.data_ptr(), dv.data_ptr(), ws.data_ptr(),
-            ws_bytes, B, Hq, Hkv, N, D, int(causal), mask, sp)
-
-    def step(record):
-        nk = len(KERNELS)
-        marks = [torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] if record else None
-        if record:
-            marks[0].record(stream)
-        st = lib.fa_b200_forward_strided(q.data_ptr(), sq, k.data_ptr(), skv, v.data_ptr(), skv,
-                                         o.data_ptr(), sq, lse.data_ptr(), B, Hq, Hkv, N, D,
-                                         _lib.DTYPE_FP16, int(causal), 0, None, 0, sp)
-        _lib.check(st, "fa_b200_forward_strided")
-        for i, mask in enumerate(STAGES):
-            if record:
-                marks[i + 1].record(stream)
-            _lib.check(bwd_stage(mask), "fa_b200_backward_stages")
-        if record:
-            marks[nk].record(stream)
-            step_ev.append(marks)
-
-    for _ in range(args.warmup):
-        flush.fill_(1.0)
-        step(False)
-    torch.cuda.synchronize(dev)
-    if _lib.device_error(local) != 0:
-        raise RuntimeError("device error word set during warm-up")
-
-    devices = [local]
-    with ClockSampler(devices) as clocks:
-        barrier(world)
-        torch.cuda.synchronize(dev)
-        for _ in range(args.steps):
-            flush.fill_(1.0)   # L2 flush, outside the step's events
-            step(True)
-        torch.cuda.synchronize(dev)
-        barrier(world)
-    # a GQA group split over CTAs adds the dK/dV accumulator conversion launch
-    split = (not args.deterministic and Hq > Hkv
-             and B * Hkv * ((N + 127) // 128) < 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
-    launches = (len(KERNELS) + (1 if split else 0)) * args.steps
-
-    per_kernel = {n: 0.0 for n in KERNELS}
-    total_ms = 0.0
-    for m in step_ev:
-        for i, n in enumerate(KERNELS):
-            per_kernel[n] += m[i].elapsed_time(m[i + 1])
-        total_ms += m[0].elapsed_time(m[len(KERNELS)])
-    ms = total_ms / args.steps
+    with ClockSampler([local]) as clocks:
+        ms, per_kernel = time_kernels(lib, dev, args.workload, q, k, v, do, args.steps,
+                                      args.warmup, flush, args.deterministic, None, world)
     ms = max_over_ranks(ms, world, dev)
-    per_kernel = {n: t / args.steps for n, t in per_kernel.items()}
+    launches = (n_kernels + (1 if split else 0)) * args.steps
 
     # e2e: public API, host buffers, copies inside the timed region
     pin = [t.pin_memory() for t in (q_h, k_h, v_h, do_h)]
     outs_h = [torch.empty(t.shape, dtype=torch.float16).pin_memory() for t in (q_h, k_h, v_h)]
-    dq_d = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
 
     def e2e_step():
         qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in pin)
@@ -419,28 +555,22 @@ def run_ours(args, world, rank, local):
     barrier(world)
     launches += (4 if split else 3) * args.steps   # forward, row-sum, fused backward (+ convert)
     e2e_ms = max_over_ranks(e2e_ms / args.steps, world, dev)
-    del dq_d
-    if _lib.device_error(local) != 0:
-        raise RuntimeError("device error word set during the timed steps")
+    fa_p100.check_device_errors(dev)
 
-    step_flops = 3.5 * flops_fwd(B, Hq, N, D, causal)
-    value = world * step_flops / (ms * 1e-3) / 1e12
-    e2e_value = world * step_flops / (e2e_ms * 1e-3) / 1e12
-    peak_tf, peak_gbs, peak_src = load_peak()
+    fl = step_flops(args.workload)
+    value = world * fl / (ms * 1e-3) / 1e12
+    e2e_value = world * fl / (e2e_ms * 1e-3) / 1e12
+    kernels, roofline = kernel_report(args.workload, per_kernel, peak_tf, peak_gbs, peak_src)
 
-    # roofline of the dominant kernel
-    dom = max(per_kernel, key=per_kernel.get)
-    work, unit, bound = kernel_work(dom, B, Hq, Hkv, N, D, causal)
-    t_s = per_kernel[dom] * 1e-3
-    achieved = work / t_s / (1e12 if unit == "TFLOP/s" else 1e9)
-    peak = peak_tf if unit == "TFLOP/s" else peak_gbs
-    traffic = load_traffic(args.workload).get(dom)
-    kernels = {}
-    for n in KERNELS:
-        w, u, _ = kernel_work(n, B, Hq, Hkv, N, D, causal)
-        kernels[n] = {"ms": per_kernel[n],
-                      "achieved": w / (per_kernel[n] * 1e-3) / (1e12 if u == "TFLOP/s" else 1e9),
-                      "unit": u}
+    # same-run SDPA comparison on the same inputs
+    sd_ms = max_over_ranks(time_sdpa(dev, args.workload, q, k, v, do, args.steps, args.warmup,
+                                     flush), world, dev)
+    del q, k, v, do, pin, outs_h
+    torch.cuda.empty_cache()
+
+    ring = None
+    if world > 1 and not args.no_ring:
+        ring = ring_c5(args, world, rank, local, flush)
 
     if rank != 0:
         return 0
@@ -453,22 +583,30 @@ def run_ours(args, world, rank, local):
         "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
                    "causal": causal, "inputs": f"N(0,1)*{sc} fp16, seeded",
                    "l2": "flushed (256 MiB write) between steps, outside the timed events",
-                   "parallelism": f"head-sharded x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"data-parallel replicas x{world}: each rank runs its own "
+                                   f"{args.workload} batch, no collective (weak scaling)")
+                   if world > 1 else "single GPU",
                    "backward": ("deterministic (fp16 dq, dK/dV + dQ kernels)" if args.deterministic
                                 else "fused (fp32 dq, TMA reduce-adds)"),
-                   "flops_per_step_per_gpu": step_flops,
-                   "flop_convention": "fwd 4*B*Hq*D*pairs (causal pairs N(N+1)/2), fwd+bwd 3.5x"},
+                   "flops_per_step_per_gpu": fl, "flop_convention": FLOP_CONVENTION},
         "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": sum(t.numel() * 2 for t in pin),
-                "d2h_bytes_per_step": sum(t.numel() * 2 for t in outs_h),
+                "h2d_bytes_per_step": sum(t.numel() * 2 for t in (q_h, k_h, v_h, do_h)),
+                "d2h_bytes_per_step": sum(t.numel() * 2 for t in (q_h, k_h, v_h)),
                 "path": "fa_p100.flash_attn + autograd backward, pinned host buffers"},
-        "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak,
-                     "unit": unit, "frac": achieved / peak, "traffic": traffic,
-                     "peak_source": peak_src},
+        "roofline": roofline,
         "kernels": kernels,
+        "sdpa": {"value": world * fl / (sd_ms * 1e-3) / 1e12, "ms_per_step": sd_ms,
+                 "what": "torch fp16 F.scaled_dot_product_attention fwd+bwd (default dispatch, "
+                         "enable_gqa), same inputs, L2 flush and events"},
+        "vs_sdpa": sd_ms / ms,
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if ring is not None:
+        line["ring_c5"] = ring
+    if world == 1 and not args.no_side:
+        for key, wl in SIDE_WORKLOADS.items():
+            line[key] = side_measurement(lib, dev, wl, args.steps, args.warmup, flush, peaks)
     if world == 1 and not args.no_qwen3:
         q_ms, q_loss = qwen3_step_ms(dev, "fa_p100", 5, 3)
         s_ms, s_loss = qwen3_step_ms(dev, "sdpa", 5, 3)
@@ -477,71 +615,113 @@ def run_ours(args, world, rank, local):
             "config": "BASELINE config 4: 28 layers, hidden 1024, 16/8 heads x 128, seq 8192, "
                       "B=1, fp16 autocast fwd+bwd, random init, attention via fa_p100 registration"}
     if world == 1 and not args.no_cpu_baseline:
-        cpu_tf, _, cores, sample = cpu_step_tflops(args.workload, 3, 1, min_seconds=10.0)
+        cpu_tf, cpu_ms, cores, sample = cpu_step(args.workload, 3, 1, min_seconds=10.0)
         line["cpu_baseline"] = {"value": cpu_tf, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": sample}
+                                "ms_per_step_extrapolated": cpu_ms, "sample": sample}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_ring(args, world, rank, local):
-    """Config 5: one causal sequence zigzag-sharded over the ranks, ring
-    context parallelism (fa_b200_ring). value = the whole problem's algorithmic
-    FLOPs / the max-over-ranks step time (strong scaling). At one GPU the same
-    problem runs through the single-GPU kernels, the efficiency reference."""
-    import _lib
+def ring_step_fn(world, dev, q, k, v, do):
     import fa_b200_ring as ring
     import fa_p100
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    B, Hq, Hkv, N, D, causal, sc = WORKLOADS[args.workload]
-    gen = torch.Generator(device=dev).manual_seed(100 + rank)
-    n_loc = N // world
-
-    def rnd(h):
-        return (torch.randn(B, h, n_loc, D, device=dev, generator=gen) * sc).half()
-
-    q, k, v, do = rnd(Hq).requires_grad_(True), rnd(Hkv).requires_grad_(True), \
-        rnd(Hkv).requires_grad_(True), rnd(Hq)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
 
     def step():
         for t in (q, k, v):
             t.grad = None
         o = ring.ring_flash_attn(q, k, v) if world > 1 else fa_p100.flash_attn(q, k, v, True)
         o.backward(do)
+    return step
 
-    for _ in range(args.warmup):
+
+def time_ring(world, rank, local, steps, warmup, flush, single=False):
+    """Config 5 fwd+bwd: zigzag ring over `world` ranks, or (single) the whole
+    sequence through the single-GPU kernels on this rank. Returns ms per step."""
+    dev = torch.device("cuda", local)
+    B, Hq, Hkv, N, D, causal, sc = WORKLOADS["C5"]
+    w = 1 if single else world
+    gen = torch.Generator(device=dev).manual_seed(100 + (0 if single else rank))
+    n_loc = N // w
+
+    def rnd(h):
+        return (torch.randn(B, h, n_loc, D, device=dev, generator=gen) * sc).half()
+
+    q, k, v, do = rnd(Hq).requires_grad_(True), rnd(Hkv).requires_grad_(True), \
+        rnd(Hkv).requires_grad_(True), rnd(Hq)
+    step = ring_step_fn(w, dev, q, k, v, do)
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize(dev)
-    times = []
+    if not single:
+        barrier(world)
+    total = 0.0
+    for _ in range(steps):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    if not single:
+        barrier(world)
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    return total / steps
+
+
+def ring_c5(args, world, rank, local, flush):
+    """BASELINE config 5 on the job's ranks (ring context parallelism) and, on
+    rank 0, on one GPU; strong-scaling efficiency = t1 / (world * t_world)."""
+    import fa_p100
+    dev = torch.device("cuda", local)
+    steps, warmup = min(args.steps, 5), max(3, min(args.warmup, 3))
     with ClockSampler([local]) as clocks:
-        barrier(world)
-        for _ in range(args.steps):
-            flush.fill_(1.0)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            step()
-            b.record()
-            b.synchronize()
-            times.append(a.elapsed_time(b))
-        barrier(world)
-    if _lib.device_error(local) != 0:
-        raise RuntimeError("device error word set during the ring steps")
-    ms = max_over_ranks(sum(times) / len(times), world, dev)
-    total = ring.ring_flops(B, Hq, N, D)
+        ms = max_over_ranks(time_ring(world, rank, local, steps, warmup, flush), world, dev)
+    fa_p100.check_device_errors(dev)
+    t1 = None
+    if rank == 0:
+        t1 = time_ring(world, rank, local, steps, warmup, flush, single=True)
+        fa_p100.check_device_errors(dev)
+    barrier(world)
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS["C5"]
+    total = step_flops("C5")
+    if rank != 0:
+        return None
+    peak_tf, _, _ = load_peak()
+    return {"workload": "C5", "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D, "causal": causal,
+            "parallelism": f"ring context parallel, zigzag x{world} (NCCL send/recv)",
+            "scaling": "strong", "value": total / (ms * 1e-3) / 1e12, "unit": UNIT,
+            "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "pct_of_peak_per_gpu": 100.0 * total / (ms * 1e-3) / 1e12 / world / peak_tf,
+            "single_gpu_ms_per_step": t1, "efficiency": t1 / (world * ms),
+            "l2": "flushed (256 MiB write) before each step", "clocks": clocks.summary()}
+
+
+def run_ring(args, world, rank, local):
+    """Config 5 alone (--ring): the ring over the job's ranks, strong scaling.
+    At one GPU the same problem runs through the single-GPU kernels."""
+    import fa_p100
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    with ClockSampler([local]) as clocks:
+        ms = max_over_ranks(time_ring(world, rank, local, args.steps, args.warmup, flush),
+                            world, dev)
+    fa_p100.check_device_errors(dev)
+    B, Hq, Hkv, N, D, causal, _ = WORKLOADS["C5"]
     pieces_fwd = 1 + 2 * (world - 1)
     if rank != 0:
         return 0
     peak_tf, _, peak_src = load_peak()
-    value = total / (ms * 1e-3) / 1e12
+    value = step_flops("C5") / (ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16 (fp32 accumulate)", "data": "synthetic",
         "pct_of_peak": 100.0 * value / world / peak_tf, "peak_tflops": peak_tf,
         "peak_source": peak_src,
-        "config": {"workload": args.workload, "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
+        "config": {"workload": "C5", "B": B, "Hq": Hq, "Hkv": Hkv, "N": N, "D": D,
                    "causal": causal, "parallelism": f"ring context parallel, zigzag x{world}"
                    if world > 1 else "single GPU",
                    "l2": "flushed (256 MiB write) before each step"},
@@ -556,15 +736,19 @@ def run_ring(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="C2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="C3a")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side", action="store_true",
+                    help="skip the north-star / C1 / C2 / C3a non-causal side measurements")
+    ap.add_argument("--no-ring", action="store_true",
+                    help="skip the ring_c5 measurement of multi-GPU runs")
     ap.add_argument("--deterministic", action="store_true",
                     help="time the bitwise-reproducible backward (fp16 dq, dK/dV + dQ kernels)")
     ap.add_argument("--ring", action="store_true",
-                    help="ring context parallelism over the ranks (use with --workload C5)")
+                    help="only config 5 by ring context parallelism over the ranks")
     ap.add_argument("--no-qwen3", action="store_true",
                     help="skip the Qwen3-0.6B-shaped training step (BASELINE config 4)")
     args = ap.parse_args()

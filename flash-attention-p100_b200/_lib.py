@@ -26,8 +26,7 @@ _S = Strides
 SIGNATURES = {
     "fa_b200_forward": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_forward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P,
-                                     _I, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
-    "fa_b200_forward_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
+                                     _I, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_merge_partial": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_strided": (_I, [_P, _S, _P, _S, _P, _S, _P, _S, _P, _S, _P,
                                       _P, _S, _I, _P, _S, _P, _S, _P, _SZ,
@@ -42,6 +41,8 @@ SIGNATURES = {
                                       _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_noalloc_max_rows": (_SZ, []),
     "fa_b200_device_error": (_I, [_I, _I]),
+    "fa_b200_device_error_async": (_I, [_P, _P]),
+    "fa_b200_selftest_wait": (_I, [ctypes.c_longlong, _P]),
     "fa_b200_status_string": (ctypes.c_char_p, [_I]),
     "fa_b200_last_error": (ctypes.c_char_p, []),
     "fa_b200_selftest_gemm": (_I, [_P, _P, _P, _I, _I, _I, _P]),

@@ -233,9 +233,14 @@ float* noalloc_scratch(int dev) {
   return g_noalloc_ptr[dev];
 }
 
+// Longest sequence: padded row counts (N rounded up to 128) and per-row
+// offsets stay well inside a 32-bit int.
+constexpr int kMaxN = 1 << 30;
+
 int check_shape(int B, int Hq, int Hkv, int N, int D) {
   if (D != 64 && D != 128) return FA_B200_ERR_HEAD_DIM;
   if (B < 1 || N < 1 || Hkv < 1 || Hq < 1 || Hq % Hkv != 0) return FA_B200_ERR_SHAPE;
+  if (N > kMaxN) return FA_B200_ERR_TOO_LARGE;
   return FA_B200_OK;
 }
 
@@ -529,6 +534,25 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Failure-detection self-test: thread 0 waits on a barrier nothing arrives on
+// (phase 0 of a fresh mbarrier never completes), with the kernels' own bounded
+// wait and a limit of limit_ns; it records kErrSelftest and returns. No TMA, MMA
+// or tensor memory is involved, so nothing is left in flight.
+__global__ void __launch_bounds__(32, 1) selftest_wait_kernel(unsigned long long limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    const Ctl ctl{&abort_flag, err};
+    mbar_wait_limit(smem_u32(&bar), 0, ctl, kErrSelftest, limit_ns);
+  }
+}
+
 }  // namespace fab
 
 // Shared implementation of the contiguous and strided entry points.
@@ -538,17 +562,14 @@ namespace {
 Strides from_abi(fa_b200_strides st) { return Strides{st.batch, st.head, st.row}; }
 
 int forward_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Hq,
-                 int Hkv, int N, int D, int dtype, int causal, const FwdLayout& L, void* ws,
-                 size_t ws_bytes, void* stream) {
+                 int Hkv, int N, int D, int dtype, int causal, const FwdLayout& L, void* stream) {
   if (!q || !k || !v || !o || !lse) return FA_B200_ERR_NULL_POINTER;
   int st = check_shape(B, Hq, Hkv, N, D);
   if (st != FA_B200_OK) return st;
   if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(lse) ||
-      (ws && !aligned16(ws)) || !strides_ok(L.q, 2) || !strides_ok(L.k, 2) ||
-      !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
+      !strides_ok(L.q, 2) || !strides_ok(L.k, 2) || !strides_ok(L.v, 2) || !strides_ok(L.o, 2))
     return FA_B200_ERR_ALIGNMENT;
-  (void)ws_bytes;   // the forward needs no workspace (kept in the ABI)
   int dev = 0, sms = 0;
   int* err = nullptr;
   st = device_setup(&dev, &err, &sms);
@@ -580,7 +601,7 @@ int backward_impl(const void* q, const void* k, const void* v, const void* dO, c
   if (st != FA_B200_OK) return st;
   if (dtype != FA_B200_DTYPE_FP16 && dtype != FA_B200_DTYPE_BF16) return FA_B200_ERR_DTYPE;
   if (noalloc) {
-    const size_t rows = static_cast<size_t>(B) * Hq * pad_rows(N);
+    const size_t rows = static_cast<size_t>(B) * Hq * pad_rows(N);   // N <= kMaxN: no overflow
     if (rows > kNoAllocRows) {
       set_last_error(
           "fa_b200_backward_noalloc: B*Hq*roundup(N,128) = %zu query rows exceeds the built-in "
@@ -635,24 +656,18 @@ int fa_b200_forward(const void* q, const void* k, const void* v, void* o, float*
   (void)full_precision;
   const fab::Strides sq = fab::contiguous(Hq, N, D), skv = fab::contiguous(Hkv, N, D);
   return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, FA_B200_DTYPE_FP16, causal,
-                           fab::FwdLayout{sq, skv, skv, sq}, nullptr, 0, stream);
+                           fab::FwdLayout{sq, skv, skv, sq}, stream);
 }
 
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
                             float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
-                            int causal, int full_precision, void* workspace,
-                            size_t workspace_bytes, void* stream) {
+                            int causal, int full_precision, void* stream) {
   (void)full_precision;
   return fab::forward_impl(q, k, v, o, lse, B, Hq, Hkv, N, D, dtype, causal,
                            fab::FwdLayout{fab::from_abi(sq), fab::from_abi(sk), fab::from_abi(sv),
                                           fab::from_abi(so)},
-                           workspace, workspace_bytes, stream);
-}
-
-size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal) {
-  (void)B, (void)Hq, (void)N, (void)D, (void)causal;
-  return 0;   // small grids run a kernel of their own; nothing to split or merge
+                           stream);
 }
 
 int fa_b200_merge_partial(float* o, fa_b200_strides so, float* lse, fa_b200_strides slse,
@@ -683,14 +698,14 @@ int fa_b200_merge_partial(float* o, fa_b200_strides so, float* lse, fa_b200_stri
 }
 
 size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N) {
-  if (B < 1 || Hq < 1 || N < 1) return 0;
+  if (B < 1 || Hq < 1 || N < 1 || N > fab::kMaxN) return 0;
   // Dv and LSE*log2e for every query row, each head padded to a multiple of
   // 128 rows (a multiple of 512 bytes, so the total needs no rounding).
   return 2 * static_cast<size_t>(B) * Hq * fab::pad_rows(N) * sizeof(float);
 }
 
 size_t fa_b200_backward_workspace_bytes_gqa(int B, int Hq, int Hkv, int N, int D) {
-  if (B < 1 || Hq < 1 || Hkv < 1 || N < 1 || D < 1) return 0;
+  if (B < 1 || Hq < 1 || Hkv < 1 || N < 1 || D < 1 || N > fab::kMaxN) return 0;
   // the row values, then fp32 dK and dV accumulators for a split GQA group
   return fa_b200_backward_workspace_bytes(B, Hq, N) +
          2 * static_cast<size_t>(B) * Hkv * N * D * sizeof(float);
@@ -754,6 +769,29 @@ int fa_b200_device_error(int device, int reset) {
   }
   cudaSetDevice(prev);
   return value;
+}
+
+int fa_b200_device_error_async(int* host_word, void* stream) {
+  if (!host_word) return FA_B200_ERR_NULL_POINTER;
+  int dev = 0;
+  int* err = nullptr;
+  const int st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  if (cudaMemcpyAsync(host_word, err, sizeof(int), cudaMemcpyDeviceToHost,
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return fab::launch_status("the device error word copy");
+  return FA_B200_OK;
+}
+
+int fa_b200_selftest_wait(long long limit_ns, void* stream) {
+  int dev = 0;
+  int* err = nullptr;
+  const int st = fab::device_setup(&dev, &err);
+  if (st != FA_B200_OK) return st;
+  const long long lim = std::min(std::max(limit_ns, 1000ll), 1000000000ll);
+  fab::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(lim), err);
+  return fab::launch_status("selftest_wait_kernel");
 }
 
 const char* fa_b200_last_error(void) { return fab::g_last_error; }

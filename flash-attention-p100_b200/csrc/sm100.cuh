@@ -44,6 +44,7 @@ enum DevErr : int {
   kErrTimeoutSoftmax = 3,  // softmax / compute warps waited too long for an MMA
   kErrTimeoutEpilogue = 4,
   kErrSmemAlign = 5,     // dynamic shared memory did not start 1024-byte aligned
+  kErrSelftest = 6,      // the failure-detection self-test's deliberate timeout
 };
 
 // Kernels that need every byte of shared memory do not pad for alignment:
@@ -106,9 +107,10 @@ struct Ctl {
 };
 
 // Wait for the phase with the given parity to complete. Returns false (and
-// records `code`) if the wait exceeded FAB_WAIT_LIMIT_NS, or if another role of
-// this CTA already gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Ctl& ctl, int code) {
+// records `code`) if the wait exceeded `limit_ns` of global time, or if another
+// role of this CTA already gave up.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, const Ctl& ctl,
+                                                int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -116,12 +118,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const C
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*ctl.abort_flag) return false;
-    if (globaltimer_ns() - t0 > FAB_WAIT_LIMIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *ctl.abort_flag = 1;
       if (ctl.err) atomicCAS(ctl.err, 0, code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const Ctl& ctl, int code) {
+  return mbar_wait_limit(bar, parity, ctl, code, FAB_WAIT_LIMIT_NS);
 }
 
 // After a failed wait, a producer that issued loads 0..issued-1 into a ring of

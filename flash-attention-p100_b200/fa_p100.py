@@ -90,6 +90,14 @@ def flash_attn(q, k, v, causal=False, full_precision=False):
     return _FlashAttnP100.apply(q, k, v, causal, full_precision)
 
 
+def check_device_errors(device=None):
+    """Synchronise `device` and raise RuntimeError if a kernel of this library
+    gave up a bounded internal wait since the last check (its outputs are then
+    incomplete). Each op also raises at the next call on its device once the
+    asynchronous read of the error word it enqueued has landed."""
+    _ext.check_device_errors(device)
+
+
 def _expand_kv(k, n_head):
     """K/V heads broadcast to `n_head` query heads; query head h reads kv head
     h // (n_head / Hkv) (the mapping of fa_p100.py:58-62)."""

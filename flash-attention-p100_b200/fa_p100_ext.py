@@ -16,12 +16,92 @@ these ops hand strided (B, H, N, D) views with a contiguous D axis -- e.g. the
 transposed projections an attention layer produces -- straight to the
 kernels' tensor maps; only a layout the tensor maps cannot address (an
 unaligned base or stride) is copied first.
+
+A kernel that gives up one of its bounded internal waits leaves its outputs
+incomplete and sets a device error word. Every op enqueues an asynchronous
+read of that word after its launches and raises RuntimeError at the next op
+on the device once the read has landed; `check_device_errors()` synchronises
+and raises at once.
 """
 import math
 
 import torch
 
 import _lib
+
+_DEVERR = {1: "a TMA producer waited too long for a free slot",
+           2: "the MMA issuer waited too long for an operand",
+           3: "the softmax / gradient warps waited too long for an MMA",
+           4: "an epilogue waited too long",
+           5: "dynamic shared memory was not 1024-byte aligned",
+           6: "the failure-detection self-test's deliberate timeout"}
+
+
+def _device_error_message(code):
+    return (f"an attention kernel gave up a bounded internal wait (device error {code}: "
+            f"{_DEVERR.get(code, 'unknown')}); the outputs of that call are incomplete")
+
+
+class _ErrorWatch:
+    """Per-device check of the kernels' error word without synchronising.
+
+    After each call's launches the word is copied (fa_b200_device_error_async)
+    into a pinned host int on the same stream and an event is recorded; at the
+    next call the copy is read if the event has completed, and a set word
+    raises RuntimeError there -- what the reference's AT_CUDA_CHECK after each
+    launch (fa_p100_ext.cu:81, :140) does for launch failures."""
+
+    def __init__(self, device):
+        self.device = device
+        self.word = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+    def poll(self):
+        ev = self.event
+        if ev is not None and ev.query():
+            self.event = None
+            code = int(self.word[0])
+            if code:
+                self.clear()
+                raise RuntimeError(_device_error_message(code))
+
+    def after_launch(self, stream_ptr):
+        _lib.check(_lib.lib().fa_b200_device_error_async(self.word.data_ptr(), stream_ptr),
+                   "fa_b200_device_error_async")
+        self.event = torch.cuda.Event()
+        self.event.record(torch.cuda.current_stream(self.device))
+
+    def clear(self):
+        _lib.device_error(self.device.index, reset=True)
+        self.word.zero_()
+        self.event = None
+
+
+_watches = {}
+
+
+def _watch(device):
+    w = _watches.get(device.index)
+    if w is None:
+        w = _watches[device.index] = _ErrorWatch(device)
+    return w
+
+
+def check_device_errors(device=None):
+    """Synchronise `device` (default: the current one) and raise RuntimeError if
+    a kernel of this library gave up a bounded wait since the last check; the
+    error word is cleared either way."""
+    device = torch.device("cuda", torch.cuda.current_device() if device is None
+                          else torch.device(device).index or 0)
+    code = _lib.device_error(device.index, reset=True)
+    w = _watches.get(device.index)
+    if w is not None:
+        w.word.zero_()
+        w.event = None
+    if code < 0:
+        raise RuntimeError("reading the device error word failed")
+    if code:
+        raise RuntimeError(_device_error_message(code))
 
 
 def _check_in(t, name):
@@ -88,10 +168,11 @@ def _out(t, shape, dtype, device, name):
     return t, st
 
 
-def forward(q, k, v, causal, full_precision=False, o=None):
+def forward(q, k, v, causal, full_precision=False, o=None, lse=None):
     """O (B,Hq,N,D) in q's dtype and LSE (B,Hq,N) fp32 (natural log).
     fa_p100_ext.cu:53-83. q, k, v are fp16 (the reference's type) or bf16; `o`
-    may supply the output in any layout with a contiguous D axis."""
+    may supply the output in any layout with a contiguous D axis, `lse` a
+    contiguous fp32 (B,Hq,N) buffer."""
     _check_in(q, "q")
     _check_in(k, "k")
     _check_in(v, "v")
@@ -99,14 +180,23 @@ def forward(q, k, v, causal, full_precision=False, o=None):
     B, H, Hkv, N, D = _shapes(q, k, v)
     (q, sq), (k, sk), (v, sv) = _layout(q), _layout(k), _layout(v)
     o, so = _out(o, (B, H, N, D), q.dtype, q.device, "o")
-    lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    if lse is None:
+        lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
+    elif (tuple(lse.shape) != (B, H, N) or lse.dtype != torch.float32 or lse.device != q.device
+          or not lse.is_contiguous()):
+        raise RuntimeError(f"lse must be a contiguous float32 tensor of shape {(B, H, N)} on "
+                           f"{q.device}")
     lib = _lib.lib()
+    watch = _watch(q.device)
+    watch.poll()
     with torch.cuda.device(q.device):
+        sp = _stream_ptr(q.device)
         st = lib.fa_b200_forward_strided(
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, o.data_ptr(), so,
             lse.data_ptr(), B, H, Hkv, N, D, dtype, 1 if causal else 0,
-            1 if full_precision else 0, None, 0, _stream_ptr(q.device))
-    _lib.check(st, "fa_b200_forward_strided")
+            1 if full_precision else 0, sp)
+        _lib.check(st, "fa_b200_forward_strided")
+        watch.after_launch(sp)
     return [o, lse]
 
 
@@ -140,14 +230,17 @@ def backward_into(q, k, v, dO, o, lse, causal, dq_dtype=torch.float32, dq=None, 
     lib = _lib.lib()
     ws_bytes = lib.fa_b200_backward_workspace_bytes_gqa(B, H, Hkv, N, D)
     ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
+    watch = _watch(q.device)
+    watch.poll()
     with torch.cuda.device(q.device):
+        sp = _stream_ptr(q.device)
         st = lib.fa_b200_backward_strided(
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, dO.data_ptr(), sdo,
             o.data_ptr(), so, lse.data_ptr(), dq.data_ptr(), sdq,
             1 if dq_dtype == torch.float32 else 0, dk.data_ptr(), sdk, dv.data_ptr(), sdv,
-            ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, dtype, 1 if causal else 0, 0,
-            _stream_ptr(q.device))
-    _lib.check(st, "fa_b200_backward_strided")
+            ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, dtype, 1 if causal else 0, 0, sp)
+        _lib.check(st, "fa_b200_backward_strided")
+        watch.after_launch(sp)
     return [dq, dk, dv]
 
 
@@ -176,13 +269,17 @@ def backward_accumulate(q, k, v, dO, o, lse, causal, dq, dk, dv):
     ws_bytes = lib.fa_b200_backward_workspace_bytes(B, H, N)
     ws = torch.empty((ws_bytes // 4,), device=q.device, dtype=torch.float32)
     stages = 1 | 8 | 16   # FA_B200_STAGE_ROWSUM | FUSED | ACCUMULATE
+    watch = _watch(q.device)
+    watch.poll()
     with torch.cuda.device(q.device):
+        sp = _stream_ptr(q.device)
         st = lib.fa_b200_backward_strided(
             q.data_ptr(), sq, k.data_ptr(), sk, v.data_ptr(), sv, dO.data_ptr(), sdo,
             o.data_ptr(), so, lse.data_ptr(), dq.data_ptr(), sdq, 1, dk.data_ptr(), sdk,
             dv.data_ptr(), sdv, ws.data_ptr(), ws_bytes, B, H, Hkv, N, D, dtype,
-            1 if causal else 0, stages, _stream_ptr(q.device))
-    _lib.check(st, "fa_b200_backward_strided (accumulate)")
+            1 if causal else 0, stages, sp)
+        _lib.check(st, "fa_b200_backward_strided (accumulate)")
+        watch.after_launch(sp)
     return dq, dk, dv
 
 

@@ -74,16 +74,7 @@ typedef struct fa_b200_strides {
 int fa_b200_forward_strided(const void* q, fa_b200_strides sq, const void* k, fa_b200_strides sk,
                             const void* v, fa_b200_strides sv, void* o, fa_b200_strides so,
                             float* lse, int B, int Hq, int Hkv, int N, int D, int dtype,
-                            int causal, int full_precision, void* workspace,
-                            size_t workspace_bytes, void* stream);
-
-/* Workspace fa_b200_forward_strided needs: 0. Kept for callers written against
- * an earlier version of this library, whose forward split the key range of
- * small grids and merged the halves through a workspace; small grids (B*Hq*
- * ceil(N/256) below the SM count) now run a kernel of their own with one CTA
- * per 128 query rows. fa_b200_forward_strided accepts and ignores a workspace.
- * No counterpart in the reference. */
-size_t fa_b200_forward_workspace_bytes(int B, int Hq, int N, int D, int causal);
+                            int causal, int full_precision, void* stream);
 
 /* Bytes of device workspace fa_b200_backward needs: per query row the row sum
  * Dv = rowsum(dO o O) (the reference's dvec, fa_p100_ext.cu:124) and the
@@ -181,7 +172,12 @@ int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, f
  * (a framework's caching pool, an engine that only passes its plugins the
  * tensors of the op) or a serving loop that must not call cudaMalloc, whose
  * implicit synchronisation would stall every stream on the device.
- * Same inputs, outputs and results as fa_b200_backward; the per-row workspace
+ * Same inputs, outputs and results as fa_b200_backward given the per-row
+ * workspace only (fa_b200_backward_workspace_bytes): in particular it never
+ * splits a GQA/MQA group over several CTAs, which fa_b200_backward does for
+ * small grids when given fa_b200_backward_workspace_bytes_gqa bytes -- at an
+ * MQA shape such as B=2, Hq=16, Hkv=1, N=1537 the unsplit backward is several
+ * times slower. The per-row workspace
  * goes to a 16 MiB array compiled into the library (resident on every GPU that
  * loads it until the process exits), so B*Hq*roundup(N,128) may be at most
  * fa_b200_backward_noalloc_max_rows() = 2,097,152 (FA_B200_ERR_SCRATCH_LIMIT
@@ -190,7 +186,10 @@ int fa_b200_backward_strided(const void* q, fa_b200_strides sq, const void* k, f
  * any stream capture. Every call on a device shares the one array: calls whose
  * backward passes overlap on the GPU (different streams, or different host
  * threads) race on it and must be serialised by the caller. Nothing in it has
- * to start at zero: each call writes every workspace entry it reads. */
+ * to start at zero: each call writes every workspace entry it reads. The
+ * looked-up address (like the rest of the library's per-device state) belongs
+ * to the device's primary context: after cudaDeviceReset the library must be
+ * reloaded before it is used on that device again. */
 int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const void* dO,
                              const void* o, const float* lse, void* dq, int dq_fp32, void* dk,
                              void* dv, int B, int Hq, int Hkv, int N, int D, int causal,
@@ -199,11 +198,44 @@ int fa_b200_backward_noalloc(const void* q, const void* k, const void* v, const 
 /* Largest B*Hq*roundup(N,128) fa_b200_backward_noalloc accepts. */
 size_t fa_b200_backward_noalloc_max_rows(void);
 
+/* Codes of the device error word (fa_b200_device_error). A kernel whose
+ * bounded internal wait gives up records the first code, stops its CTA without
+ * writing the rest of that CTA's outputs, and leaves the CUDA context usable:
+ * the outputs of that call are incomplete. */
+enum {
+  FA_B200_DEVERR_NONE = 0,
+  FA_B200_DEVERR_TIMEOUT_LOAD = 1,      /* a TMA producer waited too long for a free slot */
+  FA_B200_DEVERR_TIMEOUT_MMA = 2,       /* the MMA issuer waited too long for an operand */
+  FA_B200_DEVERR_TIMEOUT_COMPUTE = 3,   /* softmax / gradient warps waited too long for an MMA */
+  FA_B200_DEVERR_TIMEOUT_EPILOGUE = 4,  /* an epilogue / read-out waited too long */
+  FA_B200_DEVERR_SMEM_ALIGN = 5,        /* dynamic shared memory not 1024-byte aligned */
+  FA_B200_DEVERR_SELFTEST = 6           /* fa_b200_selftest_wait's deliberate timeout */
+};
+
 /* Reads the device error word the kernels set when a bounded internal wait
- * gives up (1..4; 0 = none) on `device`, and clears it when `reset` != 0.
- * Synchronises that device. Returns -1 if the read itself fails. Has no
- * counterpart in the reference, whose kernels have no waits. */
+ * gives up (FA_B200_DEVERR_*; 0 = none) on `device`, and clears it when
+ * `reset` != 0. Synchronises that device. Returns -1 if the read itself fails.
+ * Has no counterpart in the reference, whose kernels have no waits; it plays
+ * the part of the reference's AT_CUDA_CHECK after each launch
+ * (fa_p100_ext.cu:81, :140) for failures that happen inside a kernel. */
 int fa_b200_device_error(int device, int reset);
+
+/* Enqueues on `stream` a copy of the current device's error word into
+ * *host_word, without synchronising: the caller reads it once the stream has
+ * passed that point (an event recorded after this call). host_word should be
+ * page-locked host memory (cudaHostAlloc / a pinned tensor); pageable memory
+ * makes the copy synchronous. Lets a framework binding check every call for a
+ * kernel that gave up a wait at no synchronisation cost. No counterpart in the
+ * reference. */
+int fa_b200_device_error_async(int* host_word, void* stream);
+
+/* Failure-detection self-test, no counterpart in the reference: one thread
+ * waits on a shared-memory barrier that nothing ever arrives on, with the same
+ * bounded wait every kernel uses but a limit of `limit_ns` nanoseconds
+ * (clamped to [1 us, 1 s]); when it gives up it records FA_B200_DEVERR_SELFTEST
+ * in the device error word (if the word is still clear) and returns. Nothing
+ * else is touched, so the context stays usable. */
+int fa_b200_selftest_wait(long long limit_ns, void* stream);
 
 /* Human-readable text for a status code. */
 const char* fa_b200_status_string(int status);

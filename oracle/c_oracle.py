@@ -7,6 +7,7 @@
                         tree was available at build time.
 """
 import ctypes
+import json
 import os
 import subprocess
 
@@ -18,8 +19,21 @@ _U16 = ctypes.POINTER(ctypes.c_uint16)
 _I = ctypes.c_int
 
 
-def _make(target=None):
-    cmd = ["make", "-s", "-C", HERE] + ([target] if target else [])
+def reference_tree():
+    """The reference's source tree: $FA_REFERENCE_TREE, else BASELINE.json's
+    `reference_path`; None when neither names an existing directory."""
+    path = os.environ.get("FA_REFERENCE_TREE")
+    if not path:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                path = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            path = None
+    return path if path and os.path.isdir(path) else None
+
+
+def _make(target=None, ref=None):
+    cmd = ["make", "-s", "-C", HERE] + ([target] if target else []) + ([f"REF={ref}"] if ref else [])
     subprocess.run(cmd, check=True, capture_output=True)
 
 
@@ -35,13 +49,15 @@ def load_ours():
     return lib
 
 
-def load_reference(reference_tree="/root/reference"):
-    """The reference's own fp64 oracles, or None when they cannot be built here."""
+def load_reference(tree=None):
+    """The reference's own fp64 oracles, or None when they cannot be built here.
+    `tree` is the reference's source tree (default: reference_tree())."""
     path = os.path.join(HERE, "_ref", "libref_f64.so")
     if not os.path.exists(path):
-        if not os.path.isdir(reference_tree):
+        tree = tree or reference_tree()
+        if not tree:
             return None
-        _make("ref")
+        _make("ref", tree)
     lib = ctypes.CDLL(path)
     lib.ref_attention_f64.argtypes = [_U16, _U16, _U16, _D, _I, _I, _I, _I]
     lib.ref_bwd_f64.argtypes = [_U16] * 4 + [_D] * 3 + [_I] * 4

@@ -4,6 +4,8 @@ Run in a container that has the reference tree (it is not needed afterwards):
 
     python tests/golden/make_golden.py [/path/to/reference]
 
+(default: $FA_REFERENCE_TREE, else the `reference_path` BASELINE.json names)
+
 It imports the reference module fa_p100 (fa_p100.py) with only its JIT build of
 the sm_60 extension stubbed out (torch.utils.cpp_extension.load, fa_p100.py:21-28,
 cannot build or run without that GPU), and calls its `reference()` (fa_p100.py:65-75)
@@ -28,6 +30,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
+from oracle import c_oracle  # noqa: E402
 from oracle.attention_oracle import seeded_inputs  # noqa: E402
 
 # name: (B, Hq, Hkv, N, D, causal, seed, qk_scale)
@@ -67,7 +70,11 @@ def lse_of(q, k, causal):
     return torch.logsumexp(s, dim=-1)
 
 
-def main(ref_dir="/root/reference"):
+def main(ref_dir=None):
+    ref_dir = ref_dir or c_oracle.reference_tree()
+    if not ref_dir:
+        raise SystemExit("usage: make_golden.py <reference source tree> "
+                         "(or set FA_REFERENCE_TREE)")
     ref = import_reference(ref_dir)
     for name, (B, Hq, Hkv, N, D, causal, seed, qs) in CASES.items():
         q, k, v, do = seeded_inputs(B, Hq, Hkv, N, D, seed=seed, qk_scale=qs)

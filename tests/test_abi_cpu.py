@@ -44,6 +44,18 @@ def test_forward_argument_errors():
     assert fwd(o=MISALIGNED) == 4
 
 
+def test_sequence_length_limit():
+    # N above 2^30 is refused before any launch (padded row counts stay in int)
+    assert fwd(N=(1 << 30) + 1) == 9
+    lib = _lib.lib()
+    assert lib.fa_b200_backward_workspace_bytes(1, 1, (1 << 30) + 1) == 0
+    assert lib.fa_b200_backward_workspace_bytes(1, 1, 1 << 30) == 2 * 4 * (1 << 30)
+
+
+def test_error_word_read_needs_a_buffer():
+    assert _lib.lib().fa_b200_device_error_async(None, None) == 1
+
+
 def bwd(ws=P, ws_bytes=1 << 20, stages=None, **kw):
     a = dict(B=1, Hq=4, Hkv=2, N=16, D=64)
     a.update(kw)
@@ -105,7 +117,7 @@ def fwd_strided(sq=None, so=None, o=P, D=64, dtype=0):
     lib = _lib.lib()
     sq = sq or S()
     return lib.fa_b200_forward_strided(P, sq, P, S(2 * 16 * 64), P, S(2 * 16 * 64), o, so or S(),
-                                       P, 1, 4, 2, 16, D, dtype, 1, 0, None, 0, None)
+                                       P, 1, 4, 2, 16, D, dtype, 1, 0, None)
 
 
 def test_strided_forward_argument_errors():
@@ -180,6 +192,3 @@ def test_workspace_size_queries():
     # the GQA query adds fp32 dK and dV accumulators
     assert lib.fa_b200_backward_workspace_bytes_gqa(2, 16, 1, 1537, 64) == rows + 2 * 4 * 2 * 1 * 1537 * 64
     assert lib.fa_b200_backward_workspace_bytes_gqa(0, 16, 1, 1537, 64) == 0
-    # the forward needs no workspace: small grids run a kernel of their own
-    for shape in ((1, 8, 4096, 128, 1), (1, 32, 8192, 128, 1), (1, 2, 100, 64, 0)):
-        assert lib.fa_b200_forward_workspace_bytes(*shape) == 0

@@ -19,9 +19,17 @@ GRAD_FROB = 1e-2    # north-star gradient tolerance (Frobenius relative)
 LSE_ABS = 2e-3      # |LSE - oracle| in natural-log units
 
 
+def _nan(shape, dtype, dev):
+    """An output buffer filled with NaN before the launch, so a tile the kernel
+    never writes cannot pass by inheriting earlier correct bytes."""
+    return torch.full(shape, float("nan"), dtype=dtype, device=dev)
+
+
 def _run_fwd(q, k, v, causal, dev):
     import fa_p100_ext
-    o, lse = fa_p100_ext.forward(q.to(dev), k.to(dev), v.to(dev), causal, False)
+    B, H, N, _ = q.shape
+    o, lse = fa_p100_ext.forward(q.to(dev), k.to(dev), v.to(dev), causal, False,
+                                 o=_nan(q.shape, q.dtype, dev), lse=_nan((B, H, N), torch.float32, dev))
     torch.cuda.synchronize()
     import _lib
     assert _lib.device_error(0) == 0
@@ -36,7 +44,7 @@ def test_forward(cuda, D, Hq, Hkv, N, causal):
     q, k, v, _ = orc.seeded_inputs(1, Hq, Hkv, N, D, seed=N * 7 + D + Hkv)
     o, lse = _run_fwd(q, k, v, causal, cuda)
     ro, rlse = orc.attention(q, k, v, causal, with_lse=True)
-    assert torch.isfinite(o.float()).all()
+    assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
     e = orc.rel(o, ro)
     assert e < TOL, f"rel {e:.3e}"
     assert (lse - rlse).abs().max().item() < LSE_ABS
@@ -58,6 +66,20 @@ def test_gradients(cuda, D, Hq, Hkv, N, causal):
         r = orc.rel(got, ref)
         f = orc.frob_rel(got, ref)
         assert r < TOL and f < GRAD_FROB, f"d{name}: rel {r:.3e} frob {f:.3e}"
+    # the same gradients into NaN-filled outputs, through both backward paths
+    # (fused with fp32 dq, and the deterministic dK/dV + dQ kernels with fp16 dq)
+    import fa_p100_ext
+    qd, kd, vd, dod = (t.to(cuda) for t in (q, k, v, do))
+    o, lse = fa_p100_ext.forward(qd, kd, vd, causal)
+    for dq_dtype in (torch.float32, torch.float16):
+        dq, dk, dv = fa_p100_ext.backward_into(
+            qd, kd, vd, dod, o, lse, causal, dq_dtype, dq=_nan(qd.shape, dq_dtype, cuda),
+            dk=_nan(kd.shape, kd.dtype, cuda), dv=_nan(vd.shape, vd.dtype, cuda))
+        torch.cuda.synchronize()
+        for name, got, ref in zip("QKV", (dq, dk, dv), (rq, rk, rv)):
+            assert torch.isfinite(got.float()).all(), f"d{name} ({dq_dtype} dq): unwritten entries"
+            f = orc.frob_rel(got, ref)
+            assert f < GRAD_FROB, f"d{name} ({dq_dtype} dq): frob {f:.3e}"
 
 
 @pytest.mark.parametrize("regime", [1.0, 10.0, 0.05, 3.0])
@@ -110,8 +132,8 @@ def test_fused_stage_matches(cuda, D, causal, Hq, Hkv, N):
     q, k, v, do = (t.to(cuda) for t in orc.seeded_inputs(1, Hq, Hkv, N, D, seed=8))
     o, lse = fa_p100_ext.forward(q, k, v, causal, False)
     lib = _lib.lib()
-    dq = torch.empty(q.shape, device=cuda)
-    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    dq = _nan(q.shape, torch.float32, cuda)
+    dk, dv = _nan(k.shape, k.dtype, cuda), _nan(v.shape, v.dtype, cuda)
     ws_b = lib.fa_b200_backward_workspace_bytes(1, Hq, N)
     ws = torch.empty(ws_b // 4, device=cuda)
     st = lib.fa_b200_backward_stages(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
@@ -146,8 +168,8 @@ def test_gqa_group_split_matches_unsplit(cuda, B, Hq, Hkv, N, D):
     o, lse = fa_p100_ext.forward(q, k, v, True)
     split = fa_p100_ext.backward(q, k, v, do, o, lse, True)           # gqa-sized workspace
     lib = _lib.lib()
-    dq = torch.empty(q.shape, device="cuda")
-    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    dq = _nan(q.shape, torch.float32, cuda)
+    dk, dv = _nan(k.shape, k.dtype, cuda), _nan(v.shape, v.dtype, cuda)
     ws_bytes = lib.fa_b200_backward_workspace_bytes(B, Hq, N)          # rows only: no split
     ws = torch.empty(ws_bytes // 4, device="cuda")
     st = lib.fa_b200_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),

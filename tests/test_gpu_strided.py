@@ -53,22 +53,22 @@ def test_strided_matches_contiguous(cuda, case, layout):
     o2, lse2 = fa_p100_ext.forward(qs, ks, vs, causal)
     assert torch.equal(o, o2) and torch.equal(lse, lse2)
     # output written into a strided buffer
-    o3, _ = fa_p100_ext.forward(qs, ks, vs, causal, o=layout(torch.empty_like(q)))
+    o3, _ = fa_p100_ext.forward(qs, ks, vs, causal, o=layout(torch.full_like(q, float('nan'))))
     assert torch.equal(o, o3)
     os_ = layout(o)
     # deterministic backward (fp16 dq): every gradient bit for bit
     ref16 = fa_p100_ext.backward_into(q, k, v, do, o, lse, causal, torch.float16)
     got16 = fa_p100_ext.backward_into(qs, ks, vs, dos, os_, lse, causal, torch.float16,
-                                      layout(torch.empty_like(q)), layout(torch.empty_like(k)),
-                                      layout(torch.empty_like(v)))
+                                      layout(torch.full_like(q, float('nan'))), layout(torch.full_like(k, float('nan'))),
+                                      layout(torch.full_like(v, float('nan'))))
     for a, b in zip(ref16, got16):
         assert torch.equal(a, b)
     # fused backward (fp32 dq): dQ -- and dK/dV where a small GQA grid splits
     # its group over CTAs that add fp32 partials -- to the order of fp32 adds
     ref = fa_p100_ext.backward(q, k, v, do, o, lse, causal)
     got = fa_p100_ext.backward_into(qs, ks, vs, dos, os_, lse, causal, torch.float32,
-                                    layout(torch.empty(q.shape, device="cuda")),
-                                    layout(torch.empty_like(k)), layout(torch.empty_like(v)))
+                                    layout(torch.full(q.shape, float("nan"), device="cuda")),
+                                    layout(torch.full_like(k, float('nan'))), layout(torch.full_like(v, float('nan'))))
     for a, b in zip(ref, got):
         a, b = a.float(), b.float()
         assert (a - b).norm().item() <= 1e-3 * a.norm().item()
