@@ -24,6 +24,7 @@ on the device once the read has landed; `check_device_errors()` synchronises
 and raises at once.
 """
 import math
+import threading
 
 import torch
 
@@ -43,13 +44,16 @@ def _device_error_message(code):
 
 
 class _ErrorWatch:
-    """Per-device check of the kernels' error word without synchronising.
+    """Per-thread, per-device check of the kernels' error word without
+    synchronising.
 
     After each call's launches the word is copied (fa_b200_device_error_async)
     into a pinned host int on the same stream and an event is recorded; at the
     next call the copy is read if the event has completed, and a set word
     raises RuntimeError there -- what the reference's AT_CUDA_CHECK after each
-    launch (fa_p100_ext.cu:81, :140) does for launch failures."""
+    launch (fa_p100_ext.cu:81, :140) does for launch failures. Each host thread
+    has its own pinned word and event, so threads that drive one device from
+    several streams do not overwrite each other's copy."""
 
     def __init__(self, device):
         self.device = device
@@ -68,8 +72,9 @@ class _ErrorWatch:
     def after_launch(self, stream_ptr):
         _lib.check(_lib.lib().fa_b200_device_error_async(self.word.data_ptr(), stream_ptr),
                    "fa_b200_device_error_async")
-        self.event = torch.cuda.Event()
-        self.event.record(torch.cuda.current_stream(self.device))
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self.event = ev
 
     def clear(self):
         _lib.device_error(self.device.index, reset=True)
@@ -77,13 +82,21 @@ class _ErrorWatch:
         self.event = None
 
 
-_watches = {}
+_local = threading.local()
+
+
+def _watches():
+    d = getattr(_local, "watches", None)
+    if d is None:
+        d = _local.watches = {}
+    return d
 
 
 def _watch(device):
-    w = _watches.get(device.index)
+    ws = _watches()
+    w = ws.get(device.index)
     if w is None:
-        w = _watches[device.index] = _ErrorWatch(device)
+        w = ws[device.index] = _ErrorWatch(device)
     return w
 
 
@@ -94,7 +107,7 @@ def check_device_errors(device=None):
     device = torch.device("cuda", torch.cuda.current_device() if device is None
                           else torch.device(device).index or 0)
     code = _lib.device_error(device.index, reset=True)
-    w = _watches.get(device.index)
+    w = _watches().get(device.index)
     if w is not None:
         w.word.zero_()
         w.event = None
