@@ -21,6 +21,7 @@
 #include "../../include/fa_b200.h"
 #include "fa_bwd.cuh"
 #include "fa_fwd.cuh"
+#include "fa_fwd_persist.cuh"
 
 namespace fab {
 
@@ -77,10 +78,10 @@ void set_smem(K kernel, int bytes) {
 // dynamic shared memory.
 template <bool BF>
 void set_smem_all() {
-  set_smem(fwd_kernel<64, BF>, FwdCfg<64>::SMEM);
-  set_smem(fwd_kernel<128, BF>, FwdCfg<128>::SMEM);
   set_smem(fwd_kernel_s<64, BF>, FwdCfgS<64>::SMEM);
   set_smem(fwd_kernel_s<128, BF>, FwdCfgS<128>::SMEM);
+  set_smem(fwd_kernel_p<64, BF>, FwdCfgP<64>::SMEM);
+  set_smem(fwd_kernel_p<128, BF>, FwdCfgP<128>::SMEM);
   set_smem(bwd_dkdv_kernel<64, BF>, DkdvCfg<64>::SMEM);
   set_smem(bwd_dkdv_kernel<128, BF>, DkdvCfg<128>::SMEM);
   set_smem(bwd_dq_kernel<64, BF>, DqCfg<64>::SMEM);
@@ -261,7 +262,7 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
       !make_map4(&tk, k, dt, 2, D, N, Hkv, B, L.k, 128) ||
       !make_map4(&tv, v, dt, 2, D, N, Hkv, B, L.v, 128))
     return FA_B200_ERR_TENSOR_MAP;
-  FwdParams p;
+  FwdParams p = {};
   p.o = static_cast<uint16_t*>(o);
   p.so = L.o;
   p.lse = lse;
@@ -283,9 +284,14 @@ int launch_forward(const void* q, const void* k, const void* v, void* o, float* 
   }
   p.n_mblocks = (N + 255) / 256;
   if (p.n_mblocks > 65535) return FA_B200_ERR_TOO_LARGE;
-  fwd_kernel<D, BF><<<dim3(static_cast<unsigned>(BH), p.n_mblocks), FwdCfg<D>::THREADS,
-                      FwdCfg<D>::SMEM, stream>>>(tq, tk, tv, to, p);
-  return launch_status("fwd_kernel");
+  // persistent: one CTA per SM walks the (batch, head, m-block) items
+  const long long items = static_cast<long long>(BH) * p.n_mblocks;
+  if (items > 0x7fffffffLL) return FA_B200_ERR_TOO_LARGE;
+  p.n_items = static_cast<int>(items);
+  p.bh_count = static_cast<int>(BH);
+  const int grid = static_cast<int>(std::min<long long>(items, sms));
+  fwd_kernel_p<D, BF><<<grid, FwdCfgP<D>::THREADS, FwdCfgP<D>::SMEM, stream>>>(tq, tk, tv, to, p);
+  return launch_status("fwd_kernel_p");
 }
 
 template <int D, bool BF>

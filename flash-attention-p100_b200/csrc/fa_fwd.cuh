@@ -7,36 +7,11 @@
 // (:127-130), LSE = m + ln(l) in natural log (:321-330), GQA head mapping
 // kv_head = q_head / group (:87-92).
 //
-// Two kernels, chosen by grid size (launch_forward): fwd_kernel below, one CTA
-// per 256 query rows, when B*Hq*ceil(N/256) fills the GPU; fwd_kernel_s (further
-// down) with one CTA per 128 rows and 256-key steps when it would not.
-//
-// fwd_kernel -- structure of one CTA (one CTA = 256 query rows of one
-// (batch, q-head)):
-//   warps 0-7   softmax for query tile 0 (rows m0 .. m0+127): each warp owns
-//               16 rows; lanes i and i+16 hold columns {0..31, 64..95} and
-//               {32..63, 96..127} of row i (TMEM shape 16x32bx2)
-//   warps 8-15  softmax for query tile 1 (rows m0+128 .. m0+255), the same way
-//   warp  16    TMEM allocation + the single thread that issues tcgen05.mma
-//   warp  17    the single thread that issues TMA loads
-// Two warps per SMSP share one tile's exponentials; the two halves of a row
-// combine their partial maxima (and, at the end, row sums) with one shuffle,
-// so a tile's softmax warps meet only where P_t is handed to the MMA.
-// TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,256+D)  O1 [256+D, 256+2D)
-// P_t (fp16 pairs, column 32 + c = keys 2c, 2c+1) is written back over
-// columns 32..95 of S_t, inside S columns its warp has already read into
-// registers, in two pieces (keys 0..63, then 64..127). O_t += P_t V_j reads P_t from
-// TMEM, so P never touches shared memory, and V is the MMA's only shared operand.
-// Shared memory: Q0, Q1, a ring of K/V tiles (K_j and V_j alternate).
-//
-// Per key block j the MMA thread issues, in order,
-//   PV0_{j-1}... S0_j = Q0 K_j^T ; S1_j = Q1 K_j^T ; [P0_j] O0 += P0_j V_j ;
-//   S0_{j+1} ; [P1_j] O1 += P1_j V_j ; S1_{j+1} ; ...
-// so the tensor core computes one tile's S while the other tile's softmax runs.
-// The tensor core executes one CTA's MMAs in issue order, so S_t,j+1 overwrites
-// P_t,j only after O_t += P_t,j V_j has read it; and tcgen05.commit tracks
-// every MMA issued before it, so when softmax t sees S_t,j+1 complete, PV_t,j is
-// complete too and O_t is free to rescale.
+// Two kernels, chosen by grid size (launch_forward): fwd_kernel_p
+// (fa_fwd_persist.cuh), two 128-row query tiles per item and one persistent
+// CTA per SM walking the items, when B*Hq*ceil(N/256) fills the GPU;
+// fwd_kernel_s (below) with one CTA per 128 rows and 256-key steps when it
+// would not. This file holds their shared parameters and MMA issue helpers.
 #pragma once
 #include "sm100.cuh"
 
@@ -54,28 +29,8 @@ struct FwdParams {
   int n_mblocks;    // m-blocks of the launched kernel: ceil(N / 256), or ceil(N / 128)
                     // for the small-grid kernel
   float scale_log2; // softmax scale * log2(e)
-};
-
-template <int D>
-struct FwdCfg {
-  static constexpr int BM = 128;                // rows per query tile
-  static constexpr int BN = 128;                // keys per block
-  static constexpr int CH = D / 64;             // 64-column chunks per row
-  static constexpr int QBYTES = BM * D * 2;
-  static constexpr int KVBYTES = BN * D * 2;
-  static constexpr int STAGES = (D == 128) ? 4 : 8;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_RING = OFF_Q + 2 * QBYTES;
-  static constexpr int OFF_BAR = OFF_RING + STAGES * KVBYTES;
-  // barriers: q, full[STAGES], empty[STAGES], s[2], p[2][2], o[2], fin; then tmem addr + abort flag
-  static constexpr int NBAR = 1 + 2 * STAGES + 9;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // +1024 for manual alignment
-  static_assert(SMEM <= 232448, "shared memory over the per-block limit");
-  static constexpr int THREADS = 576;
-  static constexpr int MMA_WARP = 16, TMA_WARP = 17;
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t COL_S0 = 0, COL_S1 = 128, COL_O0 = 256, COL_O1 = 256 + D;
-  static constexpr uint32_t COL_P = 32;   // P pairs inside S: columns 32..95
+  int n_items;      // persistent kernel: B*Hq*n_mblocks (batch, head, m-block) items
+  int bh_count;     // B*Hq
 };
 
 }  // namespace fab
@@ -107,357 +62,6 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint3
   for (int kk = KK0; kk < KK1; ++kk)
     mma_ts(d_tmem, p_tmem + kk * 8, sdesc_add(dv, kk * 2048), idesc,
            (accumulate || kk > 0) ? 1u : 0u);
-}
-
-template <int D, bool BF>
-__global__ void __maxnreg__(96)
-    fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-               const FwdParams p) {
-  using C = FwdCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-
-  const uint32_t s_q0 = sbase + C::OFF_Q, s_q1 = s_q0 + C::QBYTES;
-  const uint32_t s_ring = sbase + C::OFF_RING;
-  const uint32_t b_q = sbase + C::OFF_BAR;
-  const uint32_t b_full = b_q + 8, b_empty = b_full + 8 * C::STAGES;
-  // b_p + 8*(2t + k): P_t's keys 0..63 (k = 0) / 64..127 (k = 1) are in TMEM
-  const uint32_t b_s = b_empty + 8 * C::STAGES, b_p = b_s + 16, b_o = b_p + 32;
-  const uint32_t b_fin = b_o + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + C::OFF_BAR + C::NBAR * 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (B*Hq, m-blocks): every head's longest causal rows are dispatched first
-  const int bh = blockIdx.x;
-  const int mb = p.n_mblocks - 1 - static_cast<int>(blockIdx.y);
-  const int m0 = mb * 256;
-  // tensor-map coordinates: query head / batch, and the kv head it reads
-  const int b_i = bh / p.hq, hq_i = bh % p.hq, hk_i = hq_i / p.group;
-  const int nblk = (p.n + 127) / 128;
-  int ntile[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int r0 = m0 + 128 * t;
-    ntile[t] = (r0 >= p.n) ? 0 : (p.causal ? min(nblk, r0 / 128 + 1) : nblk);
-  }
-  const int nkv = max(ntile[0], ntile[1]);
-  const Ctl ctl{abort_flag, p.err};
-
-  if (threadIdx.x == 0) {
-    mbar_init(b_q, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(b_full + 8 * s, 1);
-      mbar_init(b_empty + 8 * s, 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(b_s + 8 * t, 1);
-      mbar_init(b_p + 16 * t, 256);
-      mbar_init(b_p + 16 * t + 8, 256);
-      mbar_init(b_o + 8 * t, 1);
-    }
-    mbar_init(b_fin, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == C::MMA_WARP) tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == C::TMA_WARP) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(b_q, 2 * C::QBYTES);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int c = 0; c < C::CH; ++c)
-          tma_load_4d((t ? s_q1 : s_q0) + c * 16384, &tm_q, b_q, c * 64, m0 + 128 * t, hq_i, b_i);
-      int it = 0;
-      bool ok = true;
-      constexpr int kAhead = 2;  // L2 prefetch distance, in key blocks
-      for (int j = 0; j < kAhead && j < nkv; ++j)
-        for (int c = 0; c < C::CH; ++c) {
-          tma_prefetch_l2_4d(&tm_k, c * 64, j * 128, hk_i, b_i);
-          tma_prefetch_l2_4d(&tm_v, c * 64, j * 128, hk_i, b_i);
-        }
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + kAhead < nkv)
-          for (int c = 0; c < C::CH; ++c) {
-            tma_prefetch_l2_4d(&tm_k, c * 64, (j + kAhead) * 128, hk_i, b_i);
-            tma_prefetch_l2_4d(&tm_v, c * 64, (j + kAhead) * 128, hk_i, b_i);
-          }
-#pragma unroll 1
-        for (int kind = 0; kind < 2 && ok; ++kind, ++it) {
-          const int slot = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          ok = mbar_wait(b_empty + 8 * slot, ph ^ 1, ctl, kErrTimeoutLoad);
-          if (!ok) break;
-          const uint32_t fb = b_full + 8 * slot;
-          mbar_arrive_expect_tx(fb, C::KVBYTES);
-          const uint32_t dst = s_ring + slot * C::KVBYTES;
-#pragma unroll
-          for (int c = 0; c < C::CH; ++c)
-            tma_load_4d(dst + c * 16384, kind ? (const void*)&tm_v : (const void*)&tm_k, fb,
-                        c * 64, j * 128, hk_i, b_i);
-        }
-      }
-      // Drain: do not leave the CTA while a load it issued may still land.
-      if (!ok) {
-        drain_loads(b_q, 1, 1);
-        drain_loads(b_full, it, C::STAGES);
-      }
-    }
-  } else if (warp == C::MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(b_q, 0, ctl, kErrTimeoutMma);
-      int it = 0;
-      if (ok && nkv > 0) {
-        // prologue: S_t,0 for both tiles
-        ok = mbar_wait(b_full, 0, ctl, kErrTimeoutMma);
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int t = 0; t < 2; ++t)
-            if (ntile[t] > 0) {
-              issue_qk<D, BF>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0, s_ring);
-              mma_commit(b_s + 8 * t);
-            }
-          mma_commit(b_empty);
-          it = 1;
-        }
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int slot_v = it % C::STAGES;
-        ok = mbar_wait(b_full + 8 * slot_v, (it / C::STAGES) & 1, ctl, kErrTimeoutMma);
-        ++it;
-        if (!ok) break;
-        tc_fence_after();
-        const bool more = (j + 1 < nkv);
-        const int slot_k = it % C::STAGES;
-        const uint32_t ph_k = (it / C::STAGES) & 1;
-        if (more) ++it;
-        bool have_k = false;
-#pragma unroll
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= ntile[t]) continue;
-          // P_t in two halves of 64 keys: the first half's products run
-          // while the softmax computes the second half's exponentials
-          ok = mbar_wait(b_p + 16 * t, j & 1, ctl, kErrTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv<D, BF, 0, 4>(tmem + (t ? C::COL_O1 : C::COL_O0),
-                                tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P,
-                                s_ring + slot_v * C::KVBYTES, j > 0);
-          ok = mbar_wait(b_p + 16 * t + 8, j & 1, ctl, kErrTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv<D, BF, 4, 8>(tmem + (t ? C::COL_O1 : C::COL_O0),
-                                tmem + (t ? C::COL_S1 : C::COL_S0) + C::COL_P,
-                                s_ring + slot_v * C::KVBYTES, true);
-          if (j + 1 < ntile[t]) {
-            if (!have_k) {
-              ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
-              if (!ok) break;
-              tc_fence_after();
-              have_k = true;
-            }
-            issue_qk<D, BF>(tmem + (t ? C::COL_S1 : C::COL_S0), t ? s_q1 : s_q0,
-                        s_ring + slot_k * C::KVBYTES);
-            mma_commit(b_s + 8 * t);
-          } else {
-            mma_commit(b_o + 8 * t);  // last block of this tile: O_t is final
-          }
-        }
-        if (!ok) break;
-        mma_commit(b_empty + 8 * slot_v);
-        if (more) {
-          if (!have_k) {
-            ok = mbar_wait(b_full + 8 * slot_k, ph_k, ctl, kErrTimeoutMma);
-            if (!ok) break;
-          }
-          mma_commit(b_empty + 8 * slot_k);
-        }
-      }
-      // Every MMA issued above must finish before TMEM is released.
-      mma_commit(b_fin);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(b_fin, 0) && globaltimer_ns() - t0 < FAB_WAIT_LIMIT_NS) {
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ softmax tile t
-    // Warp w of the tile takes the 16 rows at lanes 32*(w%4) + 16*((w>>2)&1) of
-    // its quadrant; lane i and lane i+16 share row i%16, holding its columns
-    // 32hf..32hf+31 and 64+32hf..64+32hf+31 (hf = 0, 1) through the 16x32bx2
-    // TMEM shape, so the row's maximum and sum combine with one shuffle. P goes
-    // back in two halves (keys 0..63, then 64..127), each released on its own
-    // barrier.
-    const int t = warp >> 3;
-    const int hf = lane >> 4;
-    const int r = 32 * (warp & 3) + 16 * ((warp >> 2) & 1) + (lane & 15);
-    const int row = m0 + 128 * t + r;
-    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3) + 16 * ((warp >> 2) & 1)) << 16;
-    const uint32_t t_s = tmem + (t ? C::COL_S1 : C::COL_S0) + lane_off;
-    const uint32_t t_o = tmem + (t ? C::COL_O1 : C::COL_O0) + lane_off;
-    const int nt = ntile[t];
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      ok = mbar_wait(b_s + 8 * t, j & 1, ctl, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      // s[c] is key 32*hf + c (c < 32) or 64 + 32*hf + (c - 32) of the block
-      uint32_t sr[64];
-      tmem_ld16x2_x32(t_s, reinterpret_cast<uint32_t(&)[32]>(sr[0]));
-      tmem_ld16x2_x32(t_s + 64, reinterpret_cast<uint32_t(&)[32]>(sr[32]));
-      tmem_ld_wait(sr);
-      float* s = reinterpret_cast<float*>(sr);
-      const int kb0 = j * 128;   // this step's first key
-      const int col0 = kb0 + 32 * hf;
-      const bool need_mask = (kb0 + 128 > p.n) || (p.causal && kb0 + 127 > m0 + 128 * t);
-      if (need_mask) {
-        const int lim = p.causal ? min(p.n - 1, row) : (p.n - 1);
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (col0 + c + 32 * (c / 32) > lim) s[c] = -INFINITY;
-      }
-      // this half's max: 8 interleaved chains of three-input maxima over
-      // s[16..63], seeded with s[0..15], then a tree; the other half's by shuffle
-      float mx8[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(s[c], s[c + 8]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 16)
-#pragma unroll
-        for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = max3f(mx8[k8], s[c + k8], s[c + 8 + k8]);
-      const float pmx = fmaxf(max3f(mx8[0], mx8[1], mx8[2]),
-                              max3f(max3f(mx8[3], mx8[4], mx8[5]), mx8[6], mx8[7]));
-      const float mx = fmaxf(pmx, __shfl_xor_sync(0xffffffffu, pmx, 16));
-      const float m_new = fmaxf(m_used, mx * p.scale_log2);
-      // Rescale only when the running max grew by more than 2^8: P stays
-      // below 256, and the final 1/l uses the same offset, so the result is
-      // unchanged (only which power of two the partial sums carry). Both
-      // halves see the same maxima and so take the same decision. O itself is
-      // rescaled after the exponentials (below), when S is no longer live.
-      bool rescale = false;
-      float alpha = 1.f;
-      if (j == 0) {
-        m_used = m_new;
-      } else {
-        const bool need = m_new > m_used + 8.f;
-        rescale = __any_sync(0xffffffffu, need);
-        if (need) {
-          alpha = ex2(m_used - m_new);
-          l *= alpha;
-          m_used = m_new;
-        }
-      }
-      // P = 2^(s*scale*log2e - m) on column pairs: one packed FMA and one
-      // packed add (row sum, two chains of pairs) per two columns. Pair
-      // column COL_P + k/2 holds keys k, k+1: the first 16 of this thread's
-      // pairs go to COL_P + 16*hf .. (keys 0..63 between the two threads),
-      // the rest to COL_P + 32 + 16*hf .., all inside S columns already read
-      const uint64_t sl2 = f32x2(p.scale_log2, p.scale_log2), nm = f32x2(-m_used, -m_used);
-      uint64_t lp[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
-      uint32_t w[16];
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float2 x = f32x2_split(fma_x2(f32x2(s[2 * h], s[2 * h + 1]), sl2, nm));
-        const float e0 = ex2(x.x), e1 = ex2(x.y);
-        lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
-        w[h] = pack2<BF>(e0, e1);
-      }
-      tmem_st16x2_x16(t_s + C::COL_P, w);
-      if (rescale) {   // O_t *= alpha on this thread's D/2 columns, before P_t is released
-#pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t orow[32];
-          const uint32_t a = t_o + 64 * c;   // columns 64c + 32*hf ..
-          tmem_ld16x2_x32(a, orow);
-          tmem_ld_wait(orow);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-          tmem_st16x2_x32(a, orow);
-        }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(b_p + 16 * t);   // keys 0..63 of P_t (and O_t rescaled)
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float2 x = f32x2_split(fma_x2(f32x2(s[32 + 2 * h], s[33 + 2 * h]), sl2, nm));
-        const float e0 = ex2(x.x), e1 = ex2(x.y);
-        lp[h & 1] = add_x2(lp[h & 1], f32x2(e0, e1));
-        w[h] = pack2<BF>(e0, e1);
-      }
-      tmem_st16x2_x16(t_s + C::COL_P + 32, w);
-      const float2 la = f32x2_split(add_x2(lp[0], lp[1]));
-      l += la.x + la.y;
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(b_p + 16 * t + 8);   // keys 64..127
-    }
-    if (ok && nt > 0) {
-      l += __shfl_xor_sync(0xffffffffu, l, 16);   // the row sum is the two halves' sums
-      ok = mbar_wait(b_o + 8 * t, 0, ctl, kErrTimeoutSoftmax);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        const float inv = 1.f / l;
-        const size_t bhn = static_cast<size_t>(bh) * p.n;   // LSE is (B, Hq, N) contiguous
-        // O rows rounded to 16 bits, staged as 64-column swizzled boxes over
-        // this tile's Q (every MMA that reads Q_t has completed) and written
-        // by TMA stores below
-        const uint32_t s_qt = t ? s_q1 : s_q0;
-#pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          const int col = 64 * c + 32 * hf;
-          uint32_t orow[32];
-          tmem_ld16x2_x32(t_o + 64 * c, orow);
-          tmem_ld_wait(orow);
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int piece = 4 * ((col % 64) / 32) + q4;
-            st_shared_v4(s_qt + (col / 64) * 16384 + r * 128 + ((piece ^ (r & 7)) << 4),
-                         pack2<BF>(__uint_as_float(orow[8 * q4 + 0]) * inv, __uint_as_float(orow[8 * q4 + 1]) * inv),
-                         pack2<BF>(__uint_as_float(orow[8 * q4 + 2]) * inv, __uint_as_float(orow[8 * q4 + 3]) * inv),
-                         pack2<BF>(__uint_as_float(orow[8 * q4 + 4]) * inv, __uint_as_float(orow[8 * q4 + 5]) * inv),
-                         pack2<BF>(__uint_as_float(orow[8 * q4 + 6]) * inv, __uint_as_float(orow[8 * q4 + 7]) * inv));
-          }
-        }
-        if (row < p.n && hf == 0) p.lse[bhn + row] = (m_used + __log2f(l)) * 0.69314718055994531f;
-      }
-    }
-    // every thread of the tile gets here once, whichever path it took above;
-    // a thread that skipped its staging raised the abort flag first
-    fence_async_smem();
-    named_bar_sync(1 + t, 256);
-    if ((threadIdx.x & 255) == 0 && nt > 0 && *abort_flag == 0) {
-#pragma unroll 1
-      for (int c = 0; c < D / 64; ++c)
-        tma_store_4d(&tm_o, (t ? s_q1 : s_q0) + c * 16384, 64 * c, m0 + 128 * t, hq_i, b_i);
-      bulk_commit_group();
-      bulk_wait_read_all();   // boxes read: shared memory may be released
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == C::MMA_WARP) {
-    __syncwarp();
-    tmem_dealloc(tmem, C::TMEM_COLS);
-  }
 }
 
 }  // namespace fab
@@ -713,7 +317,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < 128; ++c)
           if (kb0 + c + 64 * (c / 64) > lim) s[c] = -INFINITY;
       }
-      float mx8[8];   // as in fwd_kernel, over this half's 128 keys
+      float mx8[8];   // as in fwd_kernel_p, over this half's 128 keys
 #pragma unroll
       for (int c = 0; c < 8; ++c) mx8[c] = fmaxf(s[c], s[c + 8]);
 #pragma unroll
