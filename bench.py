@@ -306,6 +306,13 @@ def split_group(B, Hq, Hkv, N, dev):
             < 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
 
 
+def queue_ahead(cycles=200_000):
+    """A ~0.1 ms spin on the GPU before a timed step, outside its events: the
+    host enqueues the whole step meanwhile, so at small sizes (C1's step is
+    ~0.09 ms) the events time the kernels, not host launch gaps between them."""
+    torch.cuda._sleep(cycles)
+
+
 def time_kernels(lib, dev, workload, q, k, v, do, steps, warmup, flush, deterministic=False,
                  clocks=None, world=1):
     """Our kernels on resident inputs through the C ABI: per step one forward,
@@ -360,6 +367,7 @@ def time_kernels(lib, dev, workload, q, k, v, do, steps, warmup, flush, determin
         torch.cuda.synchronize(dev)
         for _ in range(steps):
             flush.fill_(1.0)   # L2 flush, outside the step's events
+            queue_ahead()
             step(True)
         torch.cuda.synchronize(dev)
         barrier(world)
@@ -404,6 +412,7 @@ def time_sdpa(dev, workload, q, k, v, do, steps, warmup, flush):
     total = 0.0
     for _ in range(steps):
         flush.fill_(1.0)
+        queue_ahead()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         step()

@@ -11,12 +11,17 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdint>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <map>
 #include <mutex>
+#include <queue>
+#include <vector>
 
 #include "../../include/fa_b200.h"
 #include "fa_bwd.cuh"
@@ -245,6 +250,83 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
   return FA_B200_OK;
 }
 
+// Fused backward CTA order: the (batch, kv-head) slices are taken in groups of
+// head_group, and inside a group causal key block 0 of every slice comes first,
+// then block 1, and so on; the GPU hands CTAs to SMs in that order as they free
+// up. Small groups keep the CTAs that run together on few slices, so their
+// Q/dO tiles and fp32 dQ rows stay in L2; but the last group's long causal
+// CTAs then start late and finish alone. fused_makespan replays that dispatch
+// (greedy, one CTA per SM) in units of query steps, a CTA costing
+// kFusedCtaFixed steps plus its own; choose_head_group weighs each candidate's
+// makespan by an L2 penalty measured on B200 (the same workload took 2.7%,
+// 4.6% and 9.2% longer per step with 1.6x, 3.2x and 6.4x the footprint of a
+// 64 MiB group at B=4, Hq=32, Hkv=8, N=3000): 3.5% per doubling past 64 MiB.
+constexpr double kFusedCtaFixed = 1.7;
+constexpr uint64_t kFusedGroupBytes = 64ull << 20;
+
+double fused_makespan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bool causal,
+                      uint64_t hg, int sms) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int s = 0; s < sms; ++s) free_at.push(0.0);
+  double end = 0.0;
+  for (uint64_t g0 = 0; g0 < bhkv; g0 += hg) {
+    const uint64_t slices = std::min(hg, bhkv - g0);
+    for (int kvb = 0; kvb < nkb; ++kvb) {
+      const int qsteps = causal ? nkb - kvb : nkb;
+      for (uint64_t s = 0; s < slices; ++s)
+        for (int sp = 0; sp < gsplit; ++sp) {
+          const int heads = std::min(gper, group - sp * gper);
+          const double t = free_at.top() + kFusedCtaFixed + static_cast<double>(heads) * qsteps;
+          free_at.pop();
+          free_at.push(t);
+          end = std::max(end, t);
+        }
+    }
+  }
+  return end;
+}
+
+// Slices per scheduling group for the fused backward; cached per shape, since
+// the replay costs up to a few milliseconds of host time for the largest grids.
+int choose_head_group(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bool causal, int N,
+                      int D, int sms) {
+  // a slice's fp32 dQ rows and 16-bit Q/dO tiles: group * N * D * 8 bytes
+  const uint64_t slice_bytes = std::max<uint64_t>(static_cast<uint64_t>(group) * N * D * 8, 1);
+  const uint64_t hg_max = std::max<uint64_t>(1, kFusedGroupBytes / slice_bytes);
+  const uint64_t n_l2 = (bhkv + hg_max - 1) / hg_max;
+  const uint64_t hg_l2 = (bhkv + n_l2 - 1) / n_l2;     // equal groups within the L2 budget
+  const uint64_t ctas = bhkv * static_cast<uint64_t>(nkb) * gsplit;
+  if (n_l2 == 1 || ctas > (1u << 16)) return static_cast<int>(hg_l2);
+  using Key = std::array<long long, 8>;
+  static std::mutex mu;
+  static std::map<Key, int> cache;
+  const Key key{static_cast<long long>(bhkv), nkb, gsplit, gper, group, causal ? 1 : 0,
+                static_cast<long long>(slice_bytes), sms};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  uint64_t best_hg = hg_l2, last = 0;
+  double best = 1e300;
+  for (uint64_t ng = n_l2; ng >= 1; --ng) {
+    const uint64_t hg = (bhkv + ng - 1) / ng;
+    if (hg == last) continue;
+    last = hg;
+    const double over = static_cast<double>(hg * slice_bytes) / static_cast<double>(kFusedGroupBytes);
+    if (over > 8.0) break;   // a penalty above 10%: larger groups cannot win
+    const double cost = fused_makespan(bhkv, nkb, gsplit, gper, group, causal, hg, sms) *
+                        (1.0 + 0.035 * std::max(0.0, std::log2(over)));
+    if (cost < best) {
+      best = cost;
+      best_hg = hg;
+    }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.emplace(key, static_cast<int>(best_hg));
+  return static_cast<int>(best_hg);
+}
+
 // The two-tile forward (256 query rows per CTA) when its grid fills the GPU,
 // else the small-grid one (128 rows per CTA, 256-key steps).
 bool forward_small_grid(int B, int Hq, int N, int sms) {
@@ -363,13 +445,6 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     CUtensorMap tdq;
     if (!make_map4(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hq, B, L.dq, 32))
       return FA_B200_ERR_TENSOR_MAP;
-    // slices per scheduling group: a (batch, kv-head) slice's fp32 dQ rows and
-    // Q/dO tiles take group * N * D * 8 bytes; a group holds at most 64 MiB of
-    // them (half of L2), and the groups are made equal in size
-    const uint64_t slice_bytes = std::max<uint64_t>(static_cast<uint64_t>(p.group) * N * D * 8, 1);
-    const uint64_t hg_max = std::max<uint64_t>(1, (64ull << 20) / slice_bytes);
-    const uint64_t n_groups = (BHkv + hg_max - 1) / hg_max;
-    p.head_group = static_cast<int>((BHkv + n_groups - 1) / n_groups);
     if (BHkv * static_cast<uint64_t>(nq128) * 16 > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
     // Too few (batch, kv-head) x key-block CTAs to fill the GPU and a GQA
     // group to divide: split each group over several CTAs, which add their
@@ -394,6 +469,7 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
       }
       p.gsplit = (p.group + p.gper - 1) / p.gper;
     }
+    p.head_group = choose_head_group(BHkv, nq128, p.gsplit, p.gper, p.group, causal != 0, N, D, sms);
     // fp32 dK / dV accumulators (32-row boxes) for the reduce-add epilogue: the
     // caller's dk/dv when accumulating, else the workspace of a split group
     CUtensorMap tdka = tdq, tdva = tdq;   // unused by the 16-bit store epilogue

@@ -958,10 +958,10 @@ __global__ void __launch_bounds__(512, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // 1-D grid over (batch, kv-head) slices x key blocks, scheduled in groups of
-  // p.head_group slices whose dQ rows and Q/dO tiles fit in L2 together; inside
-  // a group the causal key block 0 of every slice (the most work) goes first,
-  // then block 1, and so on. CTAs that run together start at neighbouring query
-  // blocks of the group's slices and advance in step, so the tiles they share
+  // p.head_group slices (the host weighs the groups' L2 footprint against the
+  // tail of long CTAs that start late); inside a group the causal key block 0
+  // of every slice (the most work) goes first, then block 1, and so on. CTAs
+  // that run together work on the group's slices, so the Q/dO tiles they share
   // and the dQ rows they add into are L2 hits rather than DRAM round trips.
   // With p.gsplit > 1 the heads of one GQA group are split over gsplit
   // consecutive CTAs (gper heads each), which add their dK/dV into fp32.
