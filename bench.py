@@ -301,11 +301,17 @@ def seeded_device_inputs(workload, dev, seed):
     return rnd(Hq), rnd(Hkv), rnd(Hkv), rnd(Hq)
 
 
-def split_group(B, Hq, Hkv, N, dev):
+def split_group(lib, B, Hq, Hkv, N, D, causal):
     """Whether the fused backward splits a GQA group (it then adds the dK/dV
-    accumulator conversion launch); the library's own rule."""
-    return (Hq > Hkv and B * Hkv * ((N + 127) // 128)
-            < 2 * torch.cuda.get_device_properties(dev).multi_processor_count)
+    accumulator conversion launch), as the library plans it for the workspace
+    the bench gives it."""
+    import ctypes
+    import _lib
+    gsplit, hg = ctypes.c_int(0), ctypes.c_int(0)
+    ws = lib.fa_b200_backward_workspace_bytes_gqa(B, Hq, Hkv, N, D)
+    _lib.check(lib.fa_b200_backward_plan(B, Hq, Hkv, N, D, int(causal), ws, ctypes.byref(gsplit),
+                                         ctypes.byref(hg)), "fa_b200_backward_plan")
+    return gsplit.value > 1
 
 
 def queue_ahead(cycles=200_000):
@@ -529,7 +535,7 @@ def run_ours(args, world, rank, local):
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
     n_kernels = 4 if args.deterministic else 3
-    split = not args.deterministic and split_group(B, Hq, Hkv, N, dev)
+    split = not args.deterministic and split_group(lib, B, Hq, Hkv, N, D, causal)
 
     with ClockSampler([local]) as clocks:
         ms, per_kernel = time_kernels(lib, dev, args.workload, q, k, v, do, args.steps,

@@ -33,6 +33,7 @@ SIGNATURES = {
                                       _I, _I, _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_workspace_bytes": (_SZ, [_I, _I, _I]),
     "fa_b200_backward_workspace_bytes_gqa": (_SZ, [_I, _I, _I, _I, _I]),
+    "fa_b200_backward_plan": (_I, [_I, _I, _I, _I, _I, _I, _SZ, _P, _P]),
     "fa_b200_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                               _I, _I, _I, _I, _I, _I, _P]),
     "fa_b200_backward_stages": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,

@@ -257,15 +257,16 @@ int check_shape(int B, int Hq, int Hkv, int N, int D) {
 // Q/dO tiles and fp32 dQ rows stay in L2; but the last group's long causal
 // CTAs then start late and finish alone. fused_makespan replays that dispatch
 // (greedy, one CTA per SM) in units of query steps, a CTA costing
-// kFusedCtaFixed steps plus its own; choose_head_group weighs each candidate's
-// makespan by an L2 penalty measured on B200 (the same workload took 2.7%,
+// kFusedCtaFixed steps (measured: 5.5 us against 3.15 us a step at D = 128)
+// plus its own; fused_plan weighs each candidate's makespan by an L2 penalty measured on B200 (the same workload took 2.7%,
 // 4.6% and 9.2% longer per step with 1.6x, 3.2x and 6.4x the footprint of a
 // 64 MiB group at B=4, Hq=32, Hkv=8, N=3000): 3.5% per doubling past 64 MiB.
 constexpr double kFusedCtaFixed = 1.7;
+constexpr double kFusedReduceEpilogue = 0.3;   // fp32 dK/dV reduce-adds instead of 16-bit stores
 constexpr uint64_t kFusedGroupBytes = 64ull << 20;
 
 double fused_makespan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bool causal,
-                      uint64_t hg, int sms) {
+                      uint64_t hg, int sms, double fixed) {
   std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
   for (int s = 0; s < sms; ++s) free_at.push(0.0);
   double end = 0.0;
@@ -276,7 +277,7 @@ double fused_makespan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, b
       for (uint64_t s = 0; s < slices; ++s)
         for (int sp = 0; sp < gsplit; ++sp) {
           const int heads = std::min(gper, group - sp * gper);
-          const double t = free_at.top() + kFusedCtaFixed + static_cast<double>(heads) * qsteps;
+          const double t = free_at.top() + fixed + static_cast<double>(heads) * qsteps;
           free_at.pop();
           free_at.push(t);
           end = std::max(end, t);
@@ -286,45 +287,105 @@ double fused_makespan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, b
   return end;
 }
 
-// Slices per scheduling group for the fused backward; cached per shape, since
-// the replay costs up to a few milliseconds of host time for the largest grids.
-int choose_head_group(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bool causal, int N,
-                      int D, int sms) {
+// Slices per scheduling group for the fused backward and the plan's cost
+// (replayed makespan x L2 penalty, in query steps; 0 when the grid is too
+// large to replay); cached per shape, since the replay costs up to a few
+// milliseconds of host time for the largest grids.
+struct FusedPlan {
+  int hg;
+  double cost;
+};
+
+FusedPlan fused_plan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bool causal, int N,
+                     int D, int sms, bool reduce_epilogue) {
   // a slice's fp32 dQ rows and 16-bit Q/dO tiles: group * N * D * 8 bytes
   const uint64_t slice_bytes = std::max<uint64_t>(static_cast<uint64_t>(group) * N * D * 8, 1);
   const uint64_t hg_max = std::max<uint64_t>(1, kFusedGroupBytes / slice_bytes);
   const uint64_t n_l2 = (bhkv + hg_max - 1) / hg_max;
   const uint64_t hg_l2 = (bhkv + n_l2 - 1) / n_l2;     // equal groups within the L2 budget
   const uint64_t ctas = bhkv * static_cast<uint64_t>(nkb) * gsplit;
-  if (n_l2 == 1 || ctas > (1u << 16)) return static_cast<int>(hg_l2);
-  using Key = std::array<long long, 8>;
+  if (ctas > (1u << 16)) return {static_cast<int>(hg_l2), 0.0};
+  const double fixed = kFusedCtaFixed + (reduce_epilogue ? kFusedReduceEpilogue : 0.0);
+  using Key = std::array<long long, 9>;
   static std::mutex mu;
-  static std::map<Key, int> cache;
+  static std::map<Key, FusedPlan> cache;
   const Key key{static_cast<long long>(bhkv), nkb, gsplit, gper, group, causal ? 1 : 0,
-                static_cast<long long>(slice_bytes), sms};
+                static_cast<long long>(slice_bytes), sms, reduce_epilogue ? 1 : 0};
   {
     std::lock_guard<std::mutex> lock(mu);
     const auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  uint64_t best_hg = hg_l2, last = 0;
-  double best = 1e300;
+  FusedPlan best{static_cast<int>(hg_l2), 1e300};
+  uint64_t last = 0;
   for (uint64_t ng = n_l2; ng >= 1; --ng) {
     const uint64_t hg = (bhkv + ng - 1) / ng;
     if (hg == last) continue;
     last = hg;
     const double over = static_cast<double>(hg * slice_bytes) / static_cast<double>(kFusedGroupBytes);
-    if (over > 8.0) break;   // a penalty above 10%: larger groups cannot win
-    const double cost = fused_makespan(bhkv, nkb, gsplit, gper, group, causal, hg, sms) *
+    if (ng < n_l2 && over > 8.0) break;   // a penalty above 10%: larger groups cannot win
+    const double cost = fused_makespan(bhkv, nkb, gsplit, gper, group, causal, hg, sms, fixed) *
                         (1.0 + 0.035 * std::max(0.0, std::log2(over)));
-    if (cost < best) {
-      best = cost;
-      best_hg = hg;
-    }
+    if (cost < best.cost) best = {static_cast<int>(hg), cost};
   }
   std::lock_guard<std::mutex> lock(mu);
-  cache.emplace(key, static_cast<int>(best_hg));
-  return static_cast<int>(best_hg);
+  cache.emplace(key, best);
+  return best;
+}
+
+// The fused backward's schedule: a GQA group may be split over gsplit CTAs of
+// gper heads each, which add their partial dK/dV into an fp32 accumulator (the
+// caller's dk/dv when accumulating, else workspace when the caller sized it
+// with fa_b200_backward_workspace_bytes_gqa: can_split); head_group slices are
+// scheduled together.
+struct FusedChoice {
+  int gsplit, gper, head_group;
+};
+
+FusedChoice choose_fused(uint64_t bhkv, int nkb, int group, bool causal, int N, int D, int sms,
+                         bool accumulate, bool can_split) {
+  FusedChoice c{1, group, 1};
+  const uint64_t units = bhkv * static_cast<uint64_t>(nkb);
+  if (group > 1 && can_split && units < 2ull * sms) {
+    // Too few (batch, kv-head) x key-block CTAs to fill the GPU. Heads per
+    // CTA: the fewest waves of CTAs times the work of each (gper heads plus a
+    // quarter head of fixed cost per CTA); more parts mean more fp32 dK/dV
+    // partials to add, which are small at these sizes.
+    double best = 1e30;
+    for (int gp = 1; gp <= group; ++gp) {
+      const uint64_t parts = (group + gp - 1) / gp;
+      const uint64_t waves = (units * parts + sms - 1) / sms;
+      const double cost = static_cast<double>(waves) * (gp + 0.25);
+      if (cost < best) {
+        best = cost;
+        c.gper = gp;
+      }
+    }
+    c.gsplit = (group + c.gper - 1) / c.gper;
+    c.head_group = fused_plan(bhkv, nkb, c.gsplit, c.gper, group, causal, N, D, sms, true).hg;
+  } else if (group > 1 && can_split && !accumulate) {
+    // A grid that fills the GPU: split the group only when the replayed
+    // makespan, with the split's accumulator memset and conversion pass
+    // (HBM-bound, ~6 TB/s) counted in query steps, comes out at least 3%
+    // shorter -- typically equal-length non-causal CTAs that leave a last
+    // wave mostly empty.
+    const double acc_bytes = 8.0 * static_cast<double>(bhkv) * N * D;
+    const double step_us = (D == 128) ? 3.15 : 1.8;
+    const double extra = (5.0 + 2.5 * acc_bytes / 6.0e6) / step_us;
+    FusedPlan best = fused_plan(bhkv, nkb, 1, group, group, causal, N, D, sms, false);
+    c.head_group = best.hg;
+    for (int parts = 2; parts <= group && best.cost > 0.0; ++parts) {
+      if (group % parts != 0) continue;
+      const FusedPlan s = fused_plan(bhkv, nkb, parts, group / parts, group, causal, N, D, sms, true);
+      if (s.cost > 0.0 && (s.cost + extra) < 0.97 * best.cost) {
+        best = {s.hg, s.cost + extra};
+        c = {parts, group / parts, s.hg};
+      }
+    }
+  } else {
+    c.head_group = fused_plan(bhkv, nkb, 1, group, group, causal, N, D, sms, accumulate).hg;
+  }
+  return c;
 }
 
 // The two-tile forward (256 query rows per CTA) when its grid fills the GPU,
@@ -446,30 +507,18 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     if (!make_map4(&tdq, dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, Hq, B, L.dq, 32))
       return FA_B200_ERR_TENSOR_MAP;
     if (BHkv * static_cast<uint64_t>(nq128) * 16 > 0x7fffffffull) return FA_B200_ERR_TOO_LARGE;
-    // Too few (batch, kv-head) x key-block CTAs to fill the GPU and a GQA
-    // group to divide: split each group over several CTAs, which add their
-    // partial dK/dV into an fp32 accumulator in the workspace (when the caller
-    // sized it with fa_b200_backward_workspace_bytes_gqa).
-    const uint64_t units = BHkv * static_cast<uint64_t>(nq128);
+    // A GQA group may be split over several CTAs, which add their partial
+    // dK/dV into an fp32 accumulator in the workspace (when the caller sized
+    // it with fa_b200_backward_workspace_bytes_gqa). With too few (batch,
+    // kv-head) x key-block CTAs to fill the GPU the split is chosen by waves;
+    // otherwise by replaying the dispatch.
     const size_t rows_bytes = 2 * sizeof(float) * static_cast<size_t>(rows_pad);
     const size_t acc_bytes = 2 * sizeof(float) * static_cast<size_t>(BHkv) * N * D;
-    if (p.group > 1 && units < 2ull * sms && (accumulate || ws_bytes >= rows_bytes + acc_bytes)) {
-      // heads per CTA: the fewest waves of CTAs times the work of each (gper
-      // heads plus a quarter head of fixed cost per CTA); more parts mean more
-      // fp32 dK/dV partials to add, which are small at these sizes
-      double best = 1e30;
-      for (int gp = 1; gp <= p.group; ++gp) {
-        const uint64_t parts = (p.group + gp - 1) / gp;
-        const uint64_t waves = (units * parts + sms - 1) / sms;
-        const double cost = static_cast<double>(waves) * (gp + 0.25);
-        if (cost < best) {
-          best = cost;
-          p.gper = gp;
-        }
-      }
-      p.gsplit = (p.group + p.gper - 1) / p.gper;
-    }
-    p.head_group = choose_head_group(BHkv, nq128, p.gsplit, p.gper, p.group, causal != 0, N, D, sms);
+    const FusedChoice fc = choose_fused(BHkv, nq128, p.group, causal != 0, N, D, sms, accumulate,
+                                        accumulate || ws_bytes >= rows_bytes + acc_bytes);
+    p.gsplit = fc.gsplit;
+    p.gper = fc.gper;
+    p.head_group = fc.head_group;
     // fp32 dK / dV accumulators (32-row boxes) for the reduce-add epilogue: the
     // caller's dk/dv when accumulating, else the workspace of a split group
     CUtensorMap tdka = tdq, tdva = tdq;   // unused by the 16-bit store epilogue
@@ -492,6 +541,7 @@ int launch_backward(const void* q, const void* k, const void* v, const void* dO,
     if (!accumulate && (!make_map4(&tdk, dk, dt, 2, D, N, Hkv, B, L.dk, 128) ||
                         !make_map4(&tdv, dv, dt, 2, D, N, Hkv, B, L.dv, 128)))
       return FA_B200_ERR_TENSOR_MAP;
+    const uint64_t units = BHkv * static_cast<uint64_t>(nq128);
     bwd_fused_kernel<D, BF><<<static_cast<unsigned>(units * p.gsplit), FusedCfg<D>::THREADS,
                               FusedCfg<D>::SMEM, stream>>>(tq, tk, tv, tdo, tdq, tdka, tdva, tdk, tdv, p);
     if (int st = launch_status("bwd_fused_kernel")) return st;
@@ -791,6 +841,23 @@ size_t fa_b200_backward_workspace_bytes_gqa(int B, int Hq, int Hkv, int N, int D
   // the row values, then fp32 dK and dV accumulators for a split GQA group
   return fa_b200_backward_workspace_bytes(B, Hq, N) +
          2 * static_cast<size_t>(B) * Hkv * N * D * sizeof(float);
+}
+
+int fa_b200_backward_plan(int B, int Hq, int Hkv, int N, int D, int causal, size_t workspace_bytes,
+                          int* gsplit, int* head_group) {
+  if (!gsplit || !head_group) return FA_B200_ERR_NULL_POINTER;
+  if (int st = fab::check_shape(B, Hq, Hkv, N, D)) return st;
+  int dev = 0, sms = 0;
+  int* err = nullptr;
+  if (int st = fab::device_setup(&dev, &err, &sms)) return st;
+  const uint64_t bhkv = static_cast<uint64_t>(B) * Hkv;
+  const size_t rows_bytes = fa_b200_backward_workspace_bytes(B, Hq, N);
+  const size_t acc_bytes = 2 * sizeof(float) * static_cast<size_t>(bhkv) * N * D;
+  const fab::FusedChoice fc = fab::choose_fused(bhkv, (N + 127) / 128, Hq / Hkv, causal != 0, N, D,
+                                                sms, false, workspace_bytes >= rows_bytes + acc_bytes);
+  *gsplit = fc.gsplit;
+  *head_group = fc.head_group;
+  return FA_B200_OK;
 }
 
 int fa_b200_backward(const void* q, const void* k, const void* v, const void* dO, const void* o,

@@ -84,12 +84,25 @@ size_t fa_b200_backward_workspace_bytes(int B, int Hq, int N);
 
 /* Workspace that also lets the fused backward split a GQA group over several
  * CTAs when B * Hkv * ceil(N/128) is too small to fill the GPU (MQA, short
- * sequences): fa_b200_backward_workspace_bytes(B, Hq, N) plus fp32 dK and dV
- * accumulators, 2 * 4 * B * Hkv * N * D bytes. Any backward given at least
- * this much may split; given less it does not. A split backward adds dK/dV
- * partials in fp32 like dQ, so their last bits too depend on the add order. No counterpart in the
- * reference, whose dK/dV are owned by one block each (flash_bwd.cuh:448-463). */
+ * sequences), or when equal-length CTAs would leave a last wave mostly empty
+ * (a replay of the CTA dispatch decides): fa_b200_backward_workspace_bytes(B,
+ * Hq, N) plus fp32 dK and dV accumulators, 2 * 4 * B * Hkv * N * D bytes. Any
+ * backward given at least this much may split; given less it does not. A split
+ * backward adds dK/dV partials in fp32 like dQ, so their last bits too depend
+ * on the add order. No counterpart in the reference, whose dK/dV are owned by
+ * one block each (flash_bwd.cuh:448-463). */
 size_t fa_b200_backward_workspace_bytes_gqa(int B, int Hq, int Hkv, int N, int D);
+
+/* The fused backward's schedule for a shape on the current device, as
+ * fa_b200_backward (dq_fp32 != 0, not accumulating) given workspace_bytes of
+ * workspace would launch it: *gsplit CTAs share each GQA group (1: unsplit;
+ * above 1 the backward also zeroes an fp32 dK/dV accumulator and launches a
+ * conversion kernel after the fused one) and *head_group (batch, kv-head)
+ * slices are scheduled together. Launches nothing. Status codes as
+ * fa_b200_backward for the shape and device checks. No counterpart in the
+ * reference, whose grid is fixed (flash_bwd.cuh:476-483). */
+int fa_b200_backward_plan(int B, int Hq, int Hkv, int N, int D, int causal, size_t workspace_bytes,
+                          int* gsplit, int* head_group);
 
 /* Backward. Replaces fa_backward (reference fa_p100_ext.cu:103-142) and
  * flash_bwd::launch (flash_bwd.cuh:466-484). Writes dq, dk and dv (fp16).

@@ -192,3 +192,16 @@ def test_workspace_size_queries():
     # the GQA query adds fp32 dK and dV accumulators
     assert lib.fa_b200_backward_workspace_bytes_gqa(2, 16, 1, 1537, 64) == rows + 2 * 4 * 2 * 1 * 1537 * 64
     assert lib.fa_b200_backward_workspace_bytes_gqa(0, 16, 1, 1537, 64) == 0
+
+
+def test_backward_plan_argument_errors():
+    """fa_b200_backward_plan checks its outputs and the shape before it looks
+    at a device."""
+    import ctypes
+    lib = _lib.lib()
+    g, h = ctypes.c_int(0), ctypes.c_int(0)
+    assert lib.fa_b200_backward_plan(1, 4, 2, 16, 64, 1, 0, None, ctypes.byref(h)) == 1
+    assert lib.fa_b200_backward_plan(1, 4, 2, 16, 64, 1, 0, ctypes.byref(g), None) == 1
+    assert lib.fa_b200_backward_plan(1, 4, 2, 16, 96, 1, 0, ctypes.byref(g), ctypes.byref(h)) == 2
+    assert lib.fa_b200_backward_plan(1, 6, 4, 16, 64, 1, 0, ctypes.byref(g), ctypes.byref(h)) == 3
+    assert lib.fa_b200_backward_plan(0, 4, 2, 16, 64, 1, 0, ctypes.byref(g), ctypes.byref(h)) == 3
