@@ -363,16 +363,17 @@ FusedChoice choose_fused(uint64_t bhkv, int nkb, int group, bool causal, int N, 
     }
     c.gsplit = (group + c.gper - 1) / c.gper;
     c.head_group = fused_plan(bhkv, nkb, c.gsplit, c.gper, group, causal, N, D, sms, true).hg;
-  } else if (group > 1 && can_split && !accumulate) {
+  } else if (group > 1 && can_split) {
     // A grid that fills the GPU: split the group only when the replayed
     // makespan, with the split's accumulator memset and conversion pass
-    // (HBM-bound, ~6 TB/s) counted in query steps, comes out at least 3%
-    // shorter -- typically equal-length non-causal CTAs that leave a last
-    // wave mostly empty.
+    // (HBM-bound, ~6 TB/s; none when the caller accumulates into fp32 dK/dV
+    // already) counted in query steps, comes out at least 3% shorter --
+    // typically equal-length non-causal CTAs that leave a last wave mostly
+    // empty, such as the 8192-row pieces of an 8-way ring.
     const double acc_bytes = 8.0 * static_cast<double>(bhkv) * N * D;
     const double step_us = (D == 128) ? 3.15 : 1.8;
-    const double extra = (5.0 + 2.5 * acc_bytes / 6.0e6) / step_us;
-    FusedPlan best = fused_plan(bhkv, nkb, 1, group, group, causal, N, D, sms, false);
+    const double extra = accumulate ? 0.0 : (5.0 + 2.5 * acc_bytes / 6.0e6) / step_us;
+    FusedPlan best = fused_plan(bhkv, nkb, 1, group, group, causal, N, D, sms, accumulate);
     c.head_group = best.hg;
     for (int parts = 2; parts <= group && best.cost > 0.0; ++parts) {
       if (group % parts != 0) continue;
