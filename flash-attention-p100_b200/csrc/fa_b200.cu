@@ -289,8 +289,8 @@ double fused_makespan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, b
 
 // Slices per scheduling group for the fused backward and the plan's cost
 // (replayed makespan x L2 penalty, in query steps; 0 when the grid is too
-// large to replay); cached per shape, since the replay costs up to a few
-// milliseconds of host time for the largest grids.
+// large to need a replay); cached per shape, since the replay costs up to a
+// few milliseconds of host time.
 struct FusedPlan {
   int hg;
   double cost;
@@ -303,8 +303,10 @@ FusedPlan fused_plan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bo
   const uint64_t hg_max = std::max<uint64_t>(1, kFusedGroupBytes / slice_bytes);
   const uint64_t n_l2 = (bhkv + hg_max - 1) / hg_max;
   const uint64_t hg_l2 = (bhkv + n_l2 - 1) / n_l2;     // equal groups within the L2 budget
+  // Past 32 waves of CTAs a late start costs the makespan under 2%: the
+  // L2-sized groups stand, without a replay.
   const uint64_t ctas = bhkv * static_cast<uint64_t>(nkb) * gsplit;
-  if (ctas > (1u << 16)) return {static_cast<int>(hg_l2), 0.0};
+  if (ctas > 32ull * static_cast<uint64_t>(sms)) return {static_cast<int>(hg_l2), 0.0};
   const double fixed = kFusedCtaFixed + (reduce_epilogue ? kFusedReduceEpilogue : 0.0);
   using Key = std::array<long long, 9>;
   static std::mutex mu;
@@ -329,6 +331,7 @@ FusedPlan fused_plan(uint64_t bhkv, int nkb, int gsplit, int gper, int group, bo
     if (cost < best.cost) best = {static_cast<int>(hg), cost};
   }
   std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() >= 4096) cache.clear();   // bounded for callers that sweep many shapes
   cache.emplace(key, best);
   return best;
 }
