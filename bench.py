@@ -24,8 +24,10 @@ Our arm (--impl ours), one JSON line from rank 0:
   sdpa      torch fp16 scaled_dot_product_attention fwd+bwd on the same inputs,
             same L2 flush and CUDA events (the reference's own comparison,
             bench_train.py:24-58);
-  north_star, c1, c2, c3a_noncausal   the same measurement (ours and SDPA) at
-            (1,32,8192,128) causal, C1, C2 and C3a non-causal (N=1 only);
+  north_star, c1, c2, c3a_noncausal, c3b, c3b_noncausal, qwen3_layer   the
+            same measurement (ours and SDPA) at (1,32,8192,128) causal, C1, C2,
+            C3a non-causal, C3b (MQA, ragged N) both ways and the Qwen3 layer
+            shape (N=1 only);
   qwen3_0p6b_step_ms   BASELINE config 4 through the HF registration vs SDPA;
   cpu_baseline  the reference's CPU path (torch fp32 eager attention, restated
             in oracle/) on one (batch, kv-head) group of the workload,
@@ -73,7 +75,8 @@ WORKLOADS = {
 }
 # measured beside the headline at N=1 (key in the JSON line: workload)
 SIDE_WORKLOADS = {"north_star": "north_star", "c1": "C1", "c2": "C2",
-                  "c3a_noncausal": "C3a_noncausal", "qwen3_layer": "qwen3_layer"}
+                  "c3a_noncausal": "C3a_noncausal", "c3b": "C3b", "c3b_noncausal": "C3b_noncausal",
+                  "qwen3_layer": "qwen3_layer"}
 FALLBACK_PEAK_TFLOPS = 1590.0
 L2_FLUSH_BYTES = 256 << 20
 FLOP_CONVENTION = "fwd 4*B*Hq*D*pairs (causal pairs N(N+1)/2), fwd+bwd 3.5x"
