@@ -16,8 +16,12 @@ Contract kept from the reference (fa_p100_hf.py:46-213):
     q_len != kv_len (a populated KV cache);
   * fp16 inputs run as they are, and so (beyond the reference) do bf16 ones;
     other dtypes (or a mix) are cast to the autocast dtype under fp16 or bf16
-    autocast, and to fp16 with a single warning outside autocast; the output is
-    cast back to the input dtype.
+    autocast, and to fp16 with a single warning outside autocast. Outside
+    autocast the output is cast back to the input dtype, as the reference does;
+    under autocast it keeps the autocast dtype, as SDPA's output does there
+    (the reference casts it back to q's dtype, fp32 for Qwen3's normed q, and the
+    o_proj that follows casts it down again: the same values, for two extra
+    elementwise passes forward and two backward per layer).
 """
 import warnings
 
@@ -69,6 +73,7 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
         is_causal = bool(getattr(module, "is_causal", True)) and query.size(2) > 1
 
     in_dtype = query.dtype
+    autocast = torch.is_autocast_enabled("cuda")
     # fp16 (the reference's type) and bf16 run as they are; anything else (fp32,
     # or a mix -- Qwen3's q/k leave their fp32 RMSNorm weights in fp32 even under
     # autocast) is cast to the autocast dtype when autocast is on, as SDPA's
@@ -76,7 +81,6 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
     native = all(t.dtype == torch.float16 for t in (query, key, value)) or all(
         t.dtype == torch.bfloat16 for t in (query, key, value))
     if not native:
-        autocast = torch.is_autocast_enabled("cuda")
         target = torch.get_autocast_dtype("cuda") if autocast else torch.float16
         if target not in (torch.float16, torch.bfloat16):
             target = torch.float16
@@ -92,7 +96,10 @@ def fa_p100_attention_forward(module, query, key, value, attention_mask, dropout
     # output straight in (B, N, H, D), the layout fa_p100_hf.py:142 transposes to
     out = flash_attn_bnhd(query, key, value, causal=bool(is_causal),
                           full_precision=getattr(module, "_fa_p100_full_precision", False))
-    return out.to(in_dtype), None
+    # under autocast the output stays in the dtype it was computed in (the
+    # consumer, o_proj, runs in that dtype too), as SDPA's does; outside
+    # autocast it goes back to the input dtype
+    return (out if autocast else out.to(in_dtype)), None
 
 
 def register():
