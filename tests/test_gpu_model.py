@@ -53,3 +53,32 @@ def test_qwen3_training_step_gradients(cuda):
     loss.backward()
     grads = [p.grad for p in m.parameters() if p.grad is not None]
     assert len(grads) > 10 and all(torch.isfinite(g).all() for g in grads)
+
+
+def test_hf_output_dtype_follows_autocast(cuda):
+    """Qwen3-style inputs (q, k fp32 after their fp32 norm weights, v fp16):
+    under autocast the backend's output keeps the autocast dtype, as SDPA's
+    does; outside autocast it returns in q's dtype. The values agree exactly."""
+    import warnings
+    import fa_p100_hf
+
+    class _Layer:
+        is_causal = True
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q = torch.randn(1, 4, 200, 64, device=cuda, generator=g)
+    k = torch.randn(1, 2, 200, 64, device=cuda, generator=g)
+    v = torch.randn(1, 2, 200, 64, device=cuda, generator=g).half()
+    with torch.autocast("cuda", dtype=torch.float16):
+        o16, _ = fa_p100_hf.fa_p100_attention_forward(_Layer(), q, k, v, None)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        ob16, _ = fa_p100_hf.fa_p100_attention_forward(_Layer(), q, k, v.bfloat16(), None)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        o32, _ = fa_p100_hf.fa_p100_attention_forward(_Layer(), q, k, v, None)
+    assert o16.dtype == torch.float16 and ob16.dtype == torch.bfloat16 and o32.dtype == torch.float32
+    assert o16.shape == (1, 200, 4, 64)
+    assert torch.equal(o16.float(), o32)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.half(), k.half().repeat_interleave(2, 1), v.repeat_interleave(2, 1), is_causal=True)
+    assert (ob16.float() - ref.transpose(1, 2).float()).abs().max().item() < 5e-2
