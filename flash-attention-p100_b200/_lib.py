@@ -8,7 +8,7 @@ loaded, importing this module raises.
 import ctypes
 import os
 
-from _build import LIB_PATH, build, up_to_date
+from _build import build, checked_requested, lib_path, up_to_date
 
 
 
@@ -43,6 +43,7 @@ SIGNATURES = {
     "fa_b200_backward_noalloc_max_rows": (_SZ, []),
     "fa_b200_device_error": (_I, [_I, _I]),
     "fa_b200_device_error_async": (_I, [_P, _P]),
+    "fa_b200_debug_tma_check": (_I, [_I, ctypes.POINTER(ctypes.c_ulonglong), _I]),
     "fa_b200_selftest_wait": (_I, [ctypes.c_longlong, _P]),
     "fa_b200_status_string": (ctypes.c_char_p, [_I]),
     "fa_b200_last_error": (ctypes.c_char_p, []),
@@ -56,12 +57,14 @@ _lib = None
 
 
 def lib():
-    """The loaded library (built on first use when needed)."""
+    """The loaded library (built on first use when needed): the release build,
+    or with FA_B200_DEBUG=1 the checked one (TMA coordinate checks,
+    fa_b200_debug_tma_check)."""
     global _lib
     if _lib is None:
         if not up_to_date():
             build()
-        handle = ctypes.CDLL(LIB_PATH)
+        handle = ctypes.CDLL(lib_path())
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.restype = res
@@ -103,5 +106,16 @@ def device_error(device=0, reset=True):
     return lib().fa_b200_device_error(int(device), 1 if reset else 0)
 
 
-def lib_path():
-    return os.path.abspath(LIB_PATH)
+def loaded_path():
+    """Path of the library this process loads (release, or checked with
+    FA_B200_DEBUG=1)."""
+    return os.path.abspath(lib_path())
+
+
+def tma_check_word(device=0, reset=True):
+    """The checked build's first TMA coordinate / alignment violation on
+    `device` (0 = none); RuntimeError from a release build."""
+    word = ctypes.c_ulonglong(0)
+    check(lib().fa_b200_debug_tma_check(int(device), ctypes.byref(word), 1 if reset else 0),
+          "fa_b200_debug_tma_check")
+    return word.value

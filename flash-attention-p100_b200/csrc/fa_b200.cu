@@ -924,6 +924,34 @@ int fa_b200_device_error(int device, int reset) {
   return value;
 }
 
+int fa_b200_debug_tma_check(int device, unsigned long long* word, int reset) {
+  if (!word) return FA_B200_ERR_NULL_POINTER;
+#ifdef FAB_CHECK_TMA
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return FA_B200_ERR_DEVICE;
+  if (cudaSetDevice(device) != cudaSuccess) return FA_B200_ERR_DEVICE;
+  int st = FA_B200_OK;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(word, fab::g_tma_check, sizeof(*word)) != cudaSuccess) {
+    fab::launch_status("reading the TMA check word");   // records the message
+    st = FA_B200_ERR_LAUNCH;
+  } else if (reset) {
+    const unsigned long long zero = 0;
+    if (cudaMemcpyToSymbol(fab::g_tma_check, &zero, sizeof(zero)) != cudaSuccess) {
+      fab::launch_status("clearing the TMA check word");
+      st = FA_B200_ERR_LAUNCH;
+    }
+  }
+  cudaSetDevice(prev);
+  return st;
+#else
+  (void)device;
+  (void)reset;
+  *word = 0;
+  return FA_B200_ERR_UNCHECKED_BUILD;
+#endif
+}
+
 int fa_b200_device_error_async(int* host_word, void* stream) {
   if (!host_word) return FA_B200_ERR_NULL_POINTER;
   int dev = 0;
@@ -963,6 +991,7 @@ const char* fa_b200_status_string(int status) {
     case FA_B200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case FA_B200_ERR_TOO_LARGE: return "problem exceeds a CUDA grid limit";
     case FA_B200_ERR_SCRATCH_LIMIT: return "problem exceeds the built-in scratch of the no-allocation backward";
+    case FA_B200_ERR_UNCHECKED_BUILD: return "not a checked build (build with FA_B200_DEBUG=1 for the TMA checks)";
     default: return "unknown status";
   }
 }

@@ -162,12 +162,49 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------
+// Checked builds (-DFAB_CHECK_TMA; `FA_B200_DEBUG=1`, see _build.py) test, before
+// every TMA copy, the rules nothing checks when the copy is issued: the
+// innermost coordinate a non-negative multiple of 8 elements (16 bytes of the
+// 16-bit maps; stricter than the 4 fp32 elements the reduce maps need, and met
+// by every column offset here), no negative coordinate on a store or a
+// reduce-add, a 128-byte aligned shared-memory box (16 bytes and a multiple of
+// 16 bytes for the untiled copy). The first violation on a device is recorded in
+// g_tma_check (fa_b200_debug_tma_check reads it) and that copy is skipped, so the
+// kernel's bounded waits end it with an error instead of the TMA unit faulting.
+// Release builds compile the checks out.
+enum TmaOp : unsigned { kTmaLoad = 1, kTmaPrefetch = 2, kTmaStore = 3, kTmaReduce = 4, kBulkLoad = 5 };
+#ifdef FAB_CHECK_TMA
+__device__ unsigned long long g_tma_check;
+// word: op << 60 | (smem misaligned) << 59 | (c0 & 0xffff) << 32 | (c1 & 0xffffffff)
+__device__ __forceinline__ bool tma_checked(unsigned op, uint32_t smem, uint32_t smem_align, int c0,
+                                            int c1, int c2, int c3) {
+  const bool to_global = op == kTmaStore || op == kTmaReduce;
+  const bool smem_bad = (smem & (smem_align - 1u)) != 0;
+  const bool bad = smem_bad || c0 < 0 || (c0 & 7) != 0 ||
+                   (to_global && (c1 < 0 || c2 < 0 || c3 < 0));
+  if (bad)
+    atomicCAS(&g_tma_check, 0ull,
+              (static_cast<unsigned long long>(op) << 60) |
+                  (static_cast<unsigned long long>(smem_bad ? 1u : 0u) << 59) |
+                  (static_cast<unsigned long long>(static_cast<uint32_t>(c0) & 0xffffu) << 32) |
+                  static_cast<unsigned long long>(static_cast<uint32_t>(c1)));
+  return !bad;
+}
+#define FAB_TMA_CHECK(op, smem, align, c0, c1, c2, c3) \
+  if (!tma_checked(op, smem, align, c0, c1, c2, c3)) return
+#else
+#define FAB_TMA_CHECK(op, smem, align, c0, c1, c2, c3) \
+  do {                                                 \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 // 3-D tiled load: coordinates are (inner column, row, head-slice).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
                                             int c1, int c2) {
+  FAB_TMA_CHECK(kTmaLoad, dst, 128u, c0, c1, c2, 0);
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
@@ -179,6 +216,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
 // tensor the kernels read is viewed as (D, N, H, B) with arbitrary strides.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
                                             int c1, int c2, int c3) {
+  FAB_TMA_CHECK(kTmaLoad, dst, 128u, c0, c1, c2, c3);
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
@@ -186,6 +224,7 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_l2_4d(const void* tmap, int c0, int c1, int c2, int c3) {
+  FAB_TMA_CHECK(kTmaPrefetch, 0u, 1u, c0, c1, c2, c3);
   asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(c0), "r"(c1), "r"(c2), "r"(c3)
@@ -196,6 +235,7 @@ __device__ __forceinline__ void tma_prefetch_l2_4d(const void* tmap, int c0, int
 // producers whose ring is too shallow to cover a DRAM round trip prefetch a
 // few steps ahead so the load into shared memory later hits L2.
 __device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int c0, int c1, int c2) {
+  FAB_TMA_CHECK(kTmaPrefetch, 0u, 1u, c0, c1, c2, 0);
   asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(c0), "r"(c1), "r"(c2)
@@ -205,6 +245,8 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int c0, int
 // 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
+  FAB_TMA_CHECK(kBulkLoad, dst | static_cast<uint32_t>(reinterpret_cast<uint64_t>(src)) | bytes, 16u,
+                0, 0, 0, 0);
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           dst),
@@ -218,6 +260,7 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 // negative. Completion is tracked with bulk groups of the issuing thread.
 __device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, uint32_t src, int c0, int c1,
                                                   int c2) {
+  FAB_TMA_CHECK(kTmaReduce, src, 128u, c0, c1, c2, 0);
   asm volatile(
       "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
       " [%0, {%1, %2, %3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
@@ -226,6 +269,7 @@ __device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, uint32_t src
 }
 __device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t src, int c0, int c1,
                                                   int c2, int c3) {
+  FAB_TMA_CHECK(kTmaReduce, src, 128u, c0, c1, c2, c3);
   asm volatile(
       "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
       " [%0, {%1, %2, %3, %4}], [%5];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
@@ -236,6 +280,7 @@ __device__ __forceinline__ void tma_reduce_add_4d(const void* tmap, uint32_t src
 // rows and columns outside the tensor are not written.
 __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int c0, int c1, int c2,
                                              int c3) {
+  FAB_TMA_CHECK(kTmaStore, src, 128u, c0, c1, c2, c3);
   asm volatile(
       "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group"
       " [%0, {%1, %2, %3, %4}], [%5];" ::"l"(reinterpret_cast<uint64_t>(tmap)),

@@ -32,9 +32,24 @@ gradients straight into the fp32 dq and travelling dK/dV accumulators
 Ops without `merge` / `bwd_acc` get the plain torch versions below.
 """
 import math
+from contextlib import contextmanager
 
 import torch
 import torch.distributed as dist
+
+
+@contextmanager
+def _step_range(on_cuda, name):
+    """An NVTX range named `name` around one ring step on CUDA tensors, so a
+    profiler timeline (nsys, ncu's NVTX filters) shows each step's exchange and
+    compute by name; nothing on CPU ranks."""
+    if on_cuda:
+        torch.cuda.nvtx.range_push(name)
+    try:
+        yield
+    finally:
+        if on_cuda:
+            torch.cuda.nvtx.range_pop()
 
 
 # ---------------------------------------------------------------------------
@@ -143,21 +158,22 @@ def ring_forward(q, k, v, ops=CudaOps, group=None):
     lse_acc = None
     kv = (k.contiguous(), v.contiguous())
     for step in range(world):
-        nxt = None
-        if step + 1 < world:
-            nxt = _exchange(kv, group, world, rank)
-        merge = getattr(ops, "merge", _merge)
-        for qh, kh, causal in ring_pieces(world, rank, step):
-            o_p, lse_p = ops.fwd(_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), causal)
-            if o_acc is None:
-                o_acc, lse_acc = o_p.float(), lse_p.float().clone()
-                continue
-            merge(_half(o_acc, qh), _half(lse_acc, qh), o_p, lse_p)
-        if nxt is not None:
-            bufs, works = nxt
-            for w in works:
-                w.wait()
-            kv = tuple(bufs)
+        with _step_range(q.is_cuda, f"ring fwd step {step}/{world}"):
+            nxt = None
+            if step + 1 < world:
+                nxt = _exchange(kv, group, world, rank)
+            merge = getattr(ops, "merge", _merge)
+            for qh, kh, causal in ring_pieces(world, rank, step):
+                o_p, lse_p = ops.fwd(_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), causal)
+                if o_acc is None:
+                    o_acc, lse_acc = o_p.float(), lse_p.float().clone()
+                    continue
+                merge(_half(o_acc, qh), _half(lse_acc, qh), o_p, lse_p)
+            if nxt is not None:
+                bufs, works = nxt
+                for w in works:
+                    w.wait()
+                kv = tuple(bufs)
     return o_acc, lse_acc
 
 
@@ -171,37 +187,38 @@ def ring_backward(q, k, v, do, o, lse, ops=CudaOps, group=None):
     acc = None           # (dK, dV) accumulators of the K/V block currently held
     acc_in = None        # accumulators in flight toward this rank
     for step in range(world):
-        nxt = None
-        if step + 1 < world:
-            nxt = _exchange(kv, group, world, rank)
-        dk_s = torch.zeros(kv[0].shape, dtype=torch.float32, device=q.device)
-        dv_s = torch.zeros_like(dk_s)
-        for qh, kh, causal in ring_pieces(world, rank, step):
-            args = (_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), _half(do, qh), _half(o, qh),
-                    _half(lse, qh), causal)
-            if hasattr(ops, "bwd_acc"):
-                ops.bwd_acc(*args, _half(dq, qh), _half(dk_s, kh), _half(dv_s, kh))
-                continue
-            dq_p, dk_p, dv_p = ops.bwd(*args)
-            _half(dq, qh).add_(dq_p)
-            _half(dk_s, kh).add_(dk_p)
-            _half(dv_s, kh).add_(dv_p)
-        # this block's accumulators arrive from the previous rank (none at step 0)
-        if acc_in is not None:
-            bufs, works = acc_in
-            for w in works:
-                w.wait()
-            dk_s.add_(bufs[0])
-            dv_s.add_(bufs[1])
-        acc = (dk_s, dv_s)
-        # pass the accumulators on with the K/V block; after the last step this
-        # hop brings them home to their owner
-        acc_in = _exchange(acc, group, world, rank)
-        if nxt is not None:
-            bufs, works = nxt
-            for w in works:
-                w.wait()
-            kv = tuple(bufs)
+        with _step_range(q.is_cuda, f"ring bwd step {step}/{world}"):
+            nxt = None
+            if step + 1 < world:
+                nxt = _exchange(kv, group, world, rank)
+            dk_s = torch.zeros(kv[0].shape, dtype=torch.float32, device=q.device)
+            dv_s = torch.zeros_like(dk_s)
+            for qh, kh, causal in ring_pieces(world, rank, step):
+                args = (_half(q, qh), _half(kv[0], kh), _half(kv[1], kh), _half(do, qh),
+                        _half(o, qh), _half(lse, qh), causal)
+                if hasattr(ops, "bwd_acc"):
+                    ops.bwd_acc(*args, _half(dq, qh), _half(dk_s, kh), _half(dv_s, kh))
+                    continue
+                dq_p, dk_p, dv_p = ops.bwd(*args)
+                _half(dq, qh).add_(dq_p)
+                _half(dk_s, kh).add_(dk_p)
+                _half(dv_s, kh).add_(dv_p)
+            # this block's accumulators arrive from the previous rank (none at step 0)
+            if acc_in is not None:
+                bufs, works = acc_in
+                for w in works:
+                    w.wait()
+                dk_s.add_(bufs[0])
+                dv_s.add_(bufs[1])
+            acc = (dk_s, dv_s)
+            # pass the accumulators on with the K/V block; after the last step this
+            # hop brings them home to their owner
+            acc_in = _exchange(acc, group, world, rank)
+            if nxt is not None:
+                bufs, works = nxt
+                for w in works:
+                    w.wait()
+                kv = tuple(bufs)
     bufs, works = acc_in
     for w in works:
         w.wait()

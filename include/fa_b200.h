@@ -39,7 +39,8 @@ enum {
   FA_B200_ERR_DEVICE = 8,          /* current device is not compute capability 10.x */
   FA_B200_ERR_TOO_LARGE = 9,       /* a grid dimension would exceed CUDA limits */
   FA_B200_ERR_SCRATCH_LIMIT = 10,  /* B*Hq*roundup(N,128) above fa_b200_backward_noalloc_max_rows() */
-  FA_B200_ERR_DTYPE = 11           /* dtype is not one of FA_B200_DTYPE_* */
+  FA_B200_ERR_DTYPE = 11,          /* dtype is not one of FA_B200_DTYPE_* */
+  FA_B200_ERR_UNCHECKED_BUILD = 12 /* fa_b200_debug_tma_check on a release build */
 };
 
 /* Element type of the 16-bit tensors (q, k, v, o, dO, dk, dv, a 16-bit dq) of
@@ -241,6 +242,21 @@ int fa_b200_device_error(int device, int reset);
  * kernel that gave up a wait at no synchronisation cost. No counterpart in the
  * reference. */
 int fa_b200_device_error_async(int* host_word, void* stream);
+
+/* Checked builds only (compiled with -DFAB_CHECK_TMA: FA_B200_DEBUG=1 when
+ * building, libfa_b200_debug.so): every TMA copy first checks its innermost
+ * coordinate (a non-negative multiple of 16 bytes), that a store or reduce-add
+ * starts at no negative coordinate, and its shared-memory alignment; the first
+ * violation on a device is recorded and that copy skipped, so the kernel ends
+ * through its bounded waits instead of the copy faulting. Writes the record for
+ * `device` to *word (0 = none; else op << 60 | smem misaligned << 59 |
+ * (inner coordinate & 0xffff) << 32 | (row coordinate & 0xffffffff), op 1 load,
+ * 2 L2 prefetch, 3 store, 4 reduce-add, 5 untiled load) and clears it when
+ * `reset` != 0; synchronises that device. Returns FA_B200_ERR_UNCHECKED_BUILD
+ * from a release build. It stands in for compute-sanitizer, which the GPU pool
+ * this was built on does not allow; no counterpart in the reference, whose
+ * kernels issue no TMA copies. */
+int fa_b200_debug_tma_check(int device, unsigned long long* word, int reset);
 
 /* Failure-detection self-test, no counterpart in the reference: one thread
  * waits on a shared-memory barrier that nothing ever arrives on, with the same

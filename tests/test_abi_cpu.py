@@ -98,11 +98,26 @@ def test_noalloc_limit_and_errors():
                                         None) == 1
 
 
+def test_release_build_has_no_tma_checks():
+    """The release library answers the checked-build query with its own status
+    (FA_B200_ERR_UNCHECKED_BUILD) and a zero word, touching no device; the
+    checked library is a separate file, loaded with FA_B200_DEBUG=1."""
+    import ctypes
+    import _build
+    if _build.checked_requested():
+        pytest.skip("this process loaded the checked library")
+    word = ctypes.c_ulonglong(7)
+    assert _lib.lib().fa_b200_debug_tma_check(0, ctypes.byref(word), 1) == 12
+    assert word.value == 0
+    assert _lib.lib().fa_b200_debug_tma_check(0, None, 1) == 1
+    assert os.path.basename(_lib.loaded_path()) == "libfa_b200.so"
+
+
 def test_selftest_rejects_unsupported_mode():
     assert _lib.lib().fa_b200_selftest_gemm(P, P, P, 1, 0, 1, None) == 3
 
 
-@pytest.mark.parametrize("code", range(0, 11))
+@pytest.mark.parametrize("code", range(0, 13))
 def test_status_strings(code):
     text = _lib.status_string(code)
     assert text and text != "unknown status"
